@@ -1,0 +1,75 @@
+"""B200 drop-in for `sa3jax.band_attention` (band_attention.py:123-180): the SAME-L decoder's fused
+differential sliding-window attention, DyT -> RoPE -> both band branches -> subtract, on sm_100a.
+
+`band_attention(qkv, q_norm, k_norm, inv_freq, num_heads, head_dim, window)` has the reference's
+signature and meaning (`q_norm`/`k_norm` are `{"alpha", "gamma", "beta"}` DyT parameters shared by both
+branches); its Pallas tiling knobs (`rows`, `halo`, `sub`, `stack`, `interpret`) are accepted and ignored:
+the sm_100a kernel tiles by 128 rows and walks only the key tiles inside the band. `ValueError` on
+unsupported shapes, as the reference. Additions: `lam` (per-pair lambda; None = 1) and the sequence-shard
+form `band_attention_shard` used with a halo exchange.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from hummingbird_b200 import _lib
+from hummingbird_b200._tensors import check_cuda, ptr, stream_handle, workspace
+
+
+def pack_norm(norm: dict, device: torch.device) -> torch.Tensor:
+    """`{"alpha": scalar, "gamma": (64,), "beta": (64,)}` -> fp32 `[alpha, gamma[64], beta[64]]`."""
+    alpha = torch.as_tensor(norm["alpha"], dtype=torch.float32, device=device).reshape(-1)[:1]
+    gamma = torch.as_tensor(norm["gamma"], dtype=torch.float32, device=device).reshape(-1)
+    beta = torch.as_tensor(norm["beta"], dtype=torch.float32, device=device).reshape(-1)
+    if gamma.numel() != 64 or beta.numel() != 64:
+        raise ValueError("DyT gamma / beta must have 64 entries (head_dim 64)")
+    return torch.cat([alpha, gamma, beta]).contiguous()
+
+
+def workspace_bytes(batch: int, rows: int, pair_count: int) -> int:
+    n = ctypes.c_size_t(0)
+    _lib.call("hb_band_workspace_bytes", batch, rows, pair_count, ctypes.byref(n))
+    return int(n.value)
+
+
+def band_attention_shard(qkv: torch.Tensor, q_norm, k_norm, inv_freq: torch.Tensor, num_heads: int,
+                         head_dim: int, window: int, *, q_begin: int, q_count: int, pos0: int,
+                         lam: torch.Tensor | None = None, pair_begin: int = 0, pair_count: int | None = None,
+                         out: torch.Tensor | None = None, ws: torch.Tensor | None = None) -> torch.Tensor:
+    """Band attention over a buffer of `rows` consecutive sequence rows (a shard plus its halos):
+    queries are buffer rows `[q_begin, q_begin + q_count)`, every buffer row is a key, and buffer row 0 sits
+    at global position `pos0`. Returns `(B, q_count, 2 * pair_count * 64)` bf16."""
+    if head_dim != 64:
+        raise ValueError(f"band_attention: need head_dim 64 (head_dim={head_dim})")
+    if qkv.dim() != 3 or qkv.dtype != torch.bfloat16 or qkv.shape[-1] != 5 * num_heads * head_dim:
+        raise ValueError(f"qkv must be bf16 (B, S, 5 * H * 64), got {tuple(qkv.shape)} {qkv.dtype}")
+    check_cuda(qkv)
+    batch, rows, _ = qkv.shape
+    pair_count = num_heads // 2 - pair_begin if pair_count is None else pair_count
+    qkv = qkv if qkv.stride(-1) == 1 and qkv.stride(0) == qkv.stride(1) * rows else qkv.contiguous()
+    qn = q_norm if isinstance(q_norm, torch.Tensor) else pack_norm(q_norm, qkv.device)
+    kn = k_norm if isinstance(k_norm, torch.Tensor) else pack_norm(k_norm, qkv.device)
+    freqs = inv_freq.to(device=qkv.device, dtype=torch.float32).contiguous()
+    if lam is not None:
+        lam = lam.to(device=qkv.device, dtype=torch.float32).contiguous()
+    if out is None:
+        out = torch.empty(batch, q_count, 2 * pair_count * head_dim, dtype=torch.bfloat16, device=qkv.device)
+    need = workspace_bytes(batch, rows, pair_count)
+    ws = workspace(need, qkv.device) if ws is None else ws
+    _lib.call("hb_band_diff_attn", ptr(qkv), qkv.stride(1), ptr(qn), ptr(kn), ptr(freqs), freqs.shape[0], ptr(lam),
+              ptr(out), out.stride(1), batch, rows, q_begin, q_count, pos0, num_heads, head_dim, window, pair_begin,
+              pair_count, ptr(ws), ws.numel(), stream_handle(qkv.device))
+    return out
+
+
+def band_attention(qkv: torch.Tensor, q_norm, k_norm, inv_freq: torch.Tensor, num_heads: int, head_dim: int,
+                   window: int, *, rows: int = 1024, halo: int = 32, sub: int = 256, stack: bool = True,
+                   interpret: bool = False, lam: torch.Tensor | None = None, out: torch.Tensor | None = None,
+                   ws: torch.Tensor | None = None) -> torch.Tensor:
+    """`(B, S, 5 * H * D)` projection output -> `(B, S, H * D)` differential band attention."""
+    del rows, halo, sub, stack, interpret  # Pallas tiling knobs of the TPU kernel
+    length = qkv.shape[1]
+    return band_attention_shard(qkv, q_norm, k_norm, inv_freq, num_heads, head_dim, window, q_begin=0,
+                                q_count=length, pos0=0, lam=lam, out=out, ws=ws)

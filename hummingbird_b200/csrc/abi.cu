@@ -1,0 +1,18 @@
+// Library-wide C-ABI entry points: version and the device status word.
+#include <cuda_runtime.h>
+
+#include "../../include/hb_b200.h"
+#include "abi_common.h"
+#include "hb_sm100.cuh"
+
+extern "C" int hb_version(void) { return 100; }
+
+extern "C" int hb_device_status(unsigned int* status_out, cudaStream_t stream) {
+  if (!status_out) return HB_ERR_NULL;
+  if (cudaStreamSynchronize(stream) != cudaSuccess) return HB_ERR_LAUNCH;
+  unsigned int v = 0, zero = 0;
+  if (cudaMemcpyFromSymbol(&v, hb::g_device_status, sizeof(v)) != cudaSuccess) return HB_ERR_LAUNCH;
+  if (v && cudaMemcpyToSymbol(hb::g_device_status, &zero, sizeof(zero)) != cudaSuccess) return HB_ERR_LAUNCH;
+  *status_out = v;
+  return HB_OK;
+}

@@ -1,0 +1,146 @@
+// SAME-L differential band attention (`band_attention`), C-ABI front end + its prologue.
+//
+// Prologue (`band_prep_kernel`): reads the `to_qkv` rows once with 128-bit loads and writes prepared tiles:
+//   q, k, q_diff, k_diff: DyT `gamma * tanh(alpha * x) + beta` in fp32, RoPE in fp32 with angles
+//                         fp32(position) * inv_freq, one bf16 cast                (band_attention.py:82-85)
+//   v:                    copied; rows past the buffer are zero                   (band_attention.py:90-94)
+// Main kernel: attn_kernel.cu in band mode: only the key tiles that intersect [q - window, q + window]
+// are visited, and scores outside |k - q| <= window or past the buffer are masked (band_attention.py:110).
+//
+// Sequence sharding: the buffer may hold halo rows from neighbouring shards. `rows` counts every row in
+// the buffer (all are real keys), `q_begin`/`q_count` select the owned query rows, and `pos0` is the
+// global position of buffer row 0, used for RoPE.
+#include <cuda_runtime.h>
+
+#include "../../include/hb_b200.h"
+#include "abi_common.h"
+#include "attn_internal.h"
+#include "prep_common.cuh"
+
+namespace hb {
+namespace {
+
+constexpr int kPrepRows = 16;
+constexpr int kPrepThreads = 256;
+
+struct BandPrepParams {
+  const uint16_t* qkv;
+  int64_t qkv_row_stride;
+  int B, rows, H_total, head0, heads;
+  const float* q_norm;
+  const float* k_norm;
+  const float* inv_freq;
+  int half;
+  int64_t pos0;
+  uint8_t* ws;
+  int ntiles;
+};
+
+__global__ void __launch_bounds__(kPrepThreads) band_prep_kernel(const BandPrepParams p) {
+  const int b = blockIdx.y;
+  const int row0 = blockIdx.x * kPrepRows;
+  const int lane = threadIdx.x & 31;
+  const int g = threadIdx.x >> 3, c = threadIdx.x & 7;
+  const unsigned gmask = 0xFFu << (lane & 24);
+  const int per_row = kSections * p.heads;
+  const int total = kPrepRows * per_row;
+  const int hc8 = p.half >> 3;
+  for (int u = g; u < total; u += kPrepThreads / 8) {
+    const int rr = u / per_row, rem = u - rr * per_row;
+    const int s = rem / p.heads, hl = rem - s * p.heads;
+    const int row = row0 + rr;
+    const bool valid = row < p.rows;
+    uint4 raw = make_uint4(0, 0, 0, 0);
+    if (valid)
+      raw = ld_nc_v4(p.qkv + ((size_t)b * p.rows + row) * p.qkv_row_stride + (size_t)s * p.H_total * kHeadDim +
+                     (size_t)(p.head0 + hl) * kHeadDim + c * 8);
+    uint4 outv = raw;
+    if (s != 2) {
+      float x[8], y[8], pv[8];
+      unpack8(raw, x);
+      const float* nrm = (s == 0 || s == 3) ? p.q_norm : p.k_norm;
+      const float alpha = __ldg(nrm);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) y[i] = fmaf(__ldg(nrm + 1 + c * 8 + i), tanhf(alpha * x[i]), __ldg(nrm + 65 + c * 8 + i));
+      const int src = (lane & 24) | rope_partner_chunk(c, hc8);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) pv[i] = __shfl_sync(gmask, y[i], src);
+      if (valid) {
+        if (c < 2 * hc8) {
+          const float pos = static_cast<float>(p.pos0 + row);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int d = c * 8 + i;
+            const float ang = pos * __ldg(p.inv_freq + (d % p.half));
+            float sn, cs;
+            sincosf(ang, &sn, &cs);
+            y[i] = y[i] * cs + pv[i] * (d < p.half ? -sn : sn);
+          }
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) y[i] = 0.f;
+      }
+      outv = pack8(y);
+    }
+    uint8_t* dst = p.ws + prep_tile_offset(b, hl, s, row / kTileRows, p.heads, p.ntiles) +
+                   sw128_offset(row % kTileRows, c);
+    *reinterpret_cast<uint4*>(dst) = outv;
+  }
+}
+
+}  // namespace
+}  // namespace hb
+
+using namespace hb;
+
+extern "C" int hb_band_workspace_bytes(int batch, int rows, int pair_count, size_t* bytes) {
+  if (!bytes) return HB_ERR_NULL;
+  if (batch < 1 || rows < 1 || pair_count < 1) return HB_ERR_SHAPE;
+  *bytes = prep_workspace_bytes(batch, rows, 2 * pair_count);
+  return HB_OK;
+}
+
+extern "C" int hb_band_diff_attn(const void* qkv, int64_t qkv_row_stride, const float* q_norm, const float* k_norm,
+                                 const float* inv_freq, int half, const float* lam, void* out,
+                                 int64_t out_row_stride, int batch, int rows, int q_begin, int q_count, int64_t pos0,
+                                 int num_heads, int head_dim, int window, int pair_begin, int pair_count,
+                                 void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  if (!qkv || !q_norm || !k_norm || !inv_freq || !out) return HB_ERR_NULL;
+  if (head_dim != kHeadDim || num_heads < 2 || num_heads % 2 || batch < 1 || rows < 1 || window < 0)
+    return HB_ERR_SHAPE;
+  if (half < 8 || half > 32 || half % 8) return HB_ERR_SHAPE;
+  if (q_begin < 0 || q_count < 1 || q_begin + q_count > rows || pos0 < 0 || pos0 + rows > (1 << 24))
+    return HB_ERR_SHAPE;
+  if (pair_begin < 0 || pair_count < 1 || pair_begin + pair_count > num_heads / 2) return HB_ERR_SHAPE;
+  if (qkv_row_stride < (int64_t)5 * num_heads * kHeadDim || out_row_stride < (int64_t)2 * pair_count * kHeadDim)
+    return HB_ERR_SHAPE;
+  if (!aligned16(qkv) || qkv_row_stride % 8 || !aligned16(out) || out_row_stride % 8 || !aligned16(workspace))
+    return HB_ERR_ALIGN;
+  const int heads = 2 * pair_count;
+  if (!workspace || workspace_bytes < prep_workspace_bytes(batch, rows, heads)) return HB_ERR_WORKSPACE;
+  int st = check_device();
+  if (st != HB_OK) return st;
+
+  const int ntiles = (rows + kTileRows - 1) / kTileRows;
+  BandPrepParams pp{static_cast<const uint16_t*>(qkv), qkv_row_stride, batch, rows, num_heads, 2 * pair_begin, heads,
+                    q_norm, k_norm, inv_freq, half, pos0, static_cast<uint8_t*>(workspace), ntiles};
+  dim3 pgrid(ntiles * (kTileRows / kPrepRows), batch);
+  band_prep_kernel<<<pgrid, kPrepThreads, 0, stream>>>(pp);
+  if (cudaGetLastError() != cudaSuccess) return HB_ERR_LAUNCH;
+
+  AttnParams ap{};
+  ap.ws = static_cast<const uint8_t*>(workspace);
+  ap.B = batch;
+  ap.rows = rows;
+  ap.ntiles = ntiles;
+  ap.heads = heads;
+  ap.q_begin = q_begin;
+  ap.q_count = q_count;
+  ap.window = window;
+  ap.lam = lam;
+  ap.lam_pair0 = pair_begin;
+  ap.out = static_cast<uint16_t*>(out);
+  ap.out_row_stride = out_row_stride;
+  return launch_diff_attention(ap, stream) == cudaSuccess ? HB_OK : HB_ERR_LAUNCH;
+}

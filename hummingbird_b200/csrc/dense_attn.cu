@@ -1,0 +1,159 @@
+// Dense differential self-attention (the DiT's `dense_attention`), C-ABI front end + its prologue.
+//
+// Prologue (`dense_prep_kernel`, HBM-bound): reads the `to_qkv` output once with 128-bit loads and writes
+// per-(batch, head, section) 128-row tiles in the SW128 UMMA image:
+//   q, k, q_diff, k_diff: RMSNorm in fp32 over the head's 64 dims -> bf16 -> RoPE in fp32 with the
+//                         caller's cos / signed-sin lane tables -> bf16   (dense_attention.py:61-69)
+//   v:                    bf16(v * mask)                                   (dense_attention.py:77)
+// The 1/sqrt(64) score scale is applied in the softmax (exact: a power of two).
+// Main kernel: attn_kernel.cu (dense mode: every key, no key mask, dense_attention.py:79-83).
+#include <cuda_runtime.h>
+
+#include "../../include/hb_b200.h"
+#include "abi_common.h"
+#include "attn_internal.h"
+#include "prep_common.cuh"
+
+namespace hb {
+namespace {
+
+constexpr int kPrepRows = 16;
+constexpr int kPrepThreads = 256;
+
+struct DensePrepParams {
+  const uint16_t* qkv;
+  int64_t qkv_row_stride;
+  int B, L, H_total, head0, heads;
+  const float* q_w;
+  const float* k_w;
+  const float* cos;
+  const float* sin;
+  int64_t table_stride;
+  const uint16_t* vmask;
+  int64_t mask_bstride, mask_lstride;
+  float eps;
+  int half;
+  uint8_t* ws;
+  int ntiles;
+};
+
+__global__ void __launch_bounds__(kPrepThreads) dense_prep_kernel(const DensePrepParams p) {
+  const int b = blockIdx.y;
+  const int row0 = blockIdx.x * kPrepRows;
+  const int lane = threadIdx.x & 31;
+  const int g = threadIdx.x >> 3, c = threadIdx.x & 7;
+  const unsigned gmask = 0xFFu << (lane & 24);
+  const int per_row = kSections * p.heads;
+  const int total = kPrepRows * per_row;
+  const int hc8 = p.half >> 3;
+  for (int u = g; u < total; u += kPrepThreads / 8) {
+    const int rr = u / per_row, rem = u - rr * per_row;
+    const int s = rem / p.heads, hl = rem - s * p.heads;
+    const int row = row0 + rr;
+    const bool valid = row < p.L;
+    uint4 raw = make_uint4(0, 0, 0, 0);
+    if (valid)
+      raw = ld_nc_v4(p.qkv + ((size_t)b * p.L + row) * p.qkv_row_stride + (size_t)s * p.H_total * kHeadDim +
+                     (size_t)(p.head0 + hl) * kHeadDim + c * 8);
+    float x[8];
+    unpack8(raw, x);
+    uint4 outv;
+    if (s == 2) {
+      const float m = valid ? __uint_as_float((uint32_t)p.vmask[b * p.mask_bstride + row * p.mask_lstride] << 16) : 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) x[i] *= m;
+      outv = pack8(x);
+    } else {
+      float ss = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ss = fmaf(x[i], x[i], ss);
+      ss += __shfl_xor_sync(gmask, ss, 1);
+      ss += __shfl_xor_sync(gmask, ss, 2);
+      ss += __shfl_xor_sync(gmask, ss, 4);
+      const float inv = rsqrtf(ss * (1.f / kHeadDim) + p.eps);
+      const float* w = (s == 0 || s == 3) ? p.q_w : p.k_w;
+      float y[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) y[i] = x[i] * inv * __ldg(w + c * 8 + i);
+      const uint4 yb = pack8(y);  // RMSNorm output rounded to bf16 (dense_attention.py:66)
+      const int src = (lane & 24) | rope_partner_chunk(c, hc8);
+      uint4 pb;
+      pb.x = __shfl_sync(gmask, yb.x, src);
+      pb.y = __shfl_sync(gmask, yb.y, src);
+      pb.z = __shfl_sync(gmask, yb.z, src);
+      pb.w = __shfl_sync(gmask, yb.w, src);
+      float yv[8], pv[8];
+      unpack8(yb, yv);
+      unpack8(pb, pv);
+      if (valid) {
+        const float* cr = p.cos + (size_t)row * p.table_stride + c * 8;
+        const float* sr = p.sin + (size_t)row * p.table_stride + c * 8;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) y[i] = yv[i] * __ldg(cr + i) + pv[i] * __ldg(sr + i);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) y[i] = 0.f;
+      }
+      outv = pack8(y);
+    }
+    uint8_t* dst = p.ws + prep_tile_offset(b, hl, s, row / kTileRows, p.heads, p.ntiles) +
+                   sw128_offset(row % kTileRows, c);
+    *reinterpret_cast<uint4*>(dst) = outv;
+  }
+}
+
+}  // namespace
+}  // namespace hb
+
+using namespace hb;
+
+extern "C" int hb_dense_workspace_bytes(int batch, int length, int pair_count, size_t* bytes) {
+  if (!bytes) return HB_ERR_NULL;
+  if (batch < 1 || length < 1 || pair_count < 1) return HB_ERR_SHAPE;
+  *bytes = prep_workspace_bytes(batch, length, 2 * pair_count);
+  return HB_OK;
+}
+
+extern "C" int hb_dense_diff_attn(const void* qkv, int64_t qkv_row_stride, const float* q_weight,
+                                  const float* k_weight, const float* cos, const float* sin, int64_t table_stride,
+                                  const void* vmask, int64_t mask_batch_stride, int64_t mask_row_stride,
+                                  const float* lam, void* out, int64_t out_row_stride, int batch, int length,
+                                  int num_heads, int head_dim, int half, float eps, int pair_begin, int pair_count,
+                                  void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  if (!qkv || !q_weight || !k_weight || !cos || !sin || !vmask || !out) return HB_ERR_NULL;
+  if (head_dim != kHeadDim || num_heads < 2 || num_heads % 2 || batch < 1 || length < 1) return HB_ERR_SHAPE;
+  if (half < 8 || half > 32 || half % 8) return HB_ERR_SHAPE;
+  if (pair_begin < 0 || pair_count < 1 || pair_begin + pair_count > num_heads / 2) return HB_ERR_SHAPE;
+  if (qkv_row_stride < (int64_t)5 * num_heads * kHeadDim || table_stride < kHeadDim ||
+      out_row_stride < (int64_t)2 * pair_count * kHeadDim)
+    return HB_ERR_SHAPE;
+  if (!aligned16(qkv) || qkv_row_stride % 8 || !aligned16(out) || out_row_stride % 8 || !aligned16(workspace))
+    return HB_ERR_ALIGN;
+  const int heads = 2 * pair_count;
+  if (!workspace || workspace_bytes < prep_workspace_bytes(batch, length, heads)) return HB_ERR_WORKSPACE;
+  int st = check_device();
+  if (st != HB_OK) return st;
+
+  const int ntiles = (length + kTileRows - 1) / kTileRows;
+  DensePrepParams pp{static_cast<const uint16_t*>(qkv), qkv_row_stride, batch, length, num_heads, 2 * pair_begin,
+                     heads, q_weight, k_weight, cos, sin, table_stride, static_cast<const uint16_t*>(vmask),
+                     mask_batch_stride, mask_row_stride, eps, half, static_cast<uint8_t*>(workspace), ntiles};
+  dim3 pgrid(ntiles * (kTileRows / kPrepRows), batch);
+  dense_prep_kernel<<<pgrid, kPrepThreads, 0, stream>>>(pp);
+  if (cudaGetLastError() != cudaSuccess) return HB_ERR_LAUNCH;
+
+  AttnParams ap{};
+  ap.ws = static_cast<const uint8_t*>(workspace);
+  ap.B = batch;
+  ap.rows = length;
+  ap.ntiles = ntiles;
+  ap.heads = heads;
+  ap.q_begin = 0;
+  ap.q_count = length;
+  ap.window = -1;
+  ap.lam = lam;
+  ap.lam_pair0 = pair_begin;
+  ap.out = static_cast<uint16_t*>(out);
+  ap.out_row_stride = out_row_stride;
+  return launch_diff_attention(ap, stream) == cudaSuccess ? HB_OK : HB_ERR_LAUNCH;
+}

@@ -1,0 +1,109 @@
+/* hummingbird-b200: C ABI of the B200 (sm_100a) kernels for hummingbird's three hot paths.
+ *
+ * Conventions for every entry point:
+ *   - plain device pointers and sizes; bf16 tensors are passed as `const void*` holding IEEE bfloat16;
+ *   - buffers are owned by the caller; nothing here allocates device memory; work that needs scratch
+ *     space takes a caller-provided workspace whose size the matching *_workspace_bytes query returns;
+ *   - every call is asynchronous on the given stream and returns an HbStatus (0 = HB_OK); an
+ *     unsupported shape returns HB_ERR_SHAPE before anything is launched (the reference raises
+ *     ValueError at trace time for the same cases);
+ *   - there is no CPU fallback: a non-sm_100 device returns HB_ERR_ARCH.
+ * The reference is kelechi-c/hummingbird (Python package `sa3jax`); citations are file:line in it.
+ */
+#ifndef HB_B200_H_
+#define HB_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+#include <cuda_runtime.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status --------------------------------------------------------------------------------------- */
+/* Values of HbStatus: see hummingbird_b200/csrc/hb_status.h (0 ok, 1 shape, 2 align, 3 arch, 4 launch,
+ * 5 device, 6 timeout, 7 workspace, 8 nccl, 9 null). */
+
+/* Library version, major * 10000 + minor * 100 + patch. */
+int hb_version(void);
+
+/* Read and clear the device status word of the current device that the kernels set when a bounded
+ * device-side wait expires (HB_ERR_TIMEOUT) or a device check fails. Synchronises `stream` first.
+ * No reference counterpart: the reference surfaces errors only as Python exceptions at trace time. */
+int hb_device_status(unsigned int* status_out, cudaStream_t stream);
+
+/* ---- dense differential self-attention (DiT) ------------------------------------------------------- */
+/* Bytes of workspace hb_dense_diff_attn needs for `pair_count` head pairs. */
+int hb_dense_workspace_bytes(int batch, int length, int pair_count, size_t* bytes);
+
+/* Replaces `sa3jax.dense_attention.dense_attention(qkv, q_weight, k_weight, cos, sin, mask, num_heads,
+ * head_dim, half, eps)` (dense_attention.py:104-153), the kernel `dit._self_attention` calls under
+ * `DiTConfig.attention == "fused"` (dit.py:185-195, config.py:57).
+ *   qkv       bf16 [batch, length, qkv_row_stride]; columns [q | k | v | q_diff | k_diff], each
+ *             num_heads * 64 wide (dense_attention.py:9-10); qkv_row_stride >= 5 * num_heads * 64.
+ *   q_weight, k_weight  fp32 [64] RMSNorm scales.
+ *   cos, sin  fp32 [length, table_stride] lane tables (`dense_attention.tables`, dense_attention.py:97-101):
+ *             column d < 64 is the cos / signed sin for head dim d; table_stride >= 64 (128 for the
+ *             reference's lane tables).
+ *   vmask     bf16 value mask, element (b, l) at vmask[b * mask_batch_stride + l * mask_row_stride].
+ *   lam       fp32 [num_heads / 2] per-pair lambda of `A - lambda * B`, or NULL for lambda = 1 (the reference).
+ *   out       bf16; row (b, l) at out + (b * length + l) * out_row_stride, pointing at the output column of
+ *             head 2 * pair_begin; 2 * pair_count * 64 columns are written.
+ *   half      rotate-half width (16 for the reference's 32-dim rotary, 32 for a full-head rotary); a
+ *             multiple of 8 in [8, 32].
+ *   pair_begin, pair_count  head-pair range computed (head-pair sharding; the full call is 0, num_heads/2).
+ * head_dim must be 64 and num_heads even (dense_attention.py:119-120). */
+int hb_dense_diff_attn(const void* qkv, int64_t qkv_row_stride, const float* q_weight, const float* k_weight,
+                       const float* cos, const float* sin, int64_t table_stride, const void* vmask,
+                       int64_t mask_batch_stride, int64_t mask_row_stride, const float* lam, void* out,
+                       int64_t out_row_stride, int batch, int length, int num_heads, int head_dim, int half,
+                       float eps, int pair_begin, int pair_count, void* workspace, size_t workspace_bytes,
+                       cudaStream_t stream);
+
+/* ---- band (sliding-window) differential attention (SAME-L decoder) --------------------------------- */
+/* Bytes of workspace hb_band_diff_attn needs for `rows` buffer rows and `pair_count` head pairs. */
+int hb_band_workspace_bytes(int batch, int rows, int pair_count, size_t* bytes);
+
+/* Replaces `sa3jax.band_attention.band_attention(qkv, q_norm, k_norm, inv_freq, num_heads, head_dim,
+ * window)` (band_attention.py:123-180), the kernel `same_l._attention` calls under
+ * `SameConfig.attention == "pallas"` (same_l.py:151-161, config.py:115).
+ *   qkv       bf16 [batch, rows, qkv_row_stride], columns as for the dense path. `rows` counts every row
+ *             in the buffer, including halo rows received from neighbouring sequence shards.
+ *   q_norm, k_norm  fp32 [129] DyT parameters {alpha, gamma[64], beta[64]} shared by both branches.
+ *   inv_freq  fp32 [half] RoPE frequencies; angles are fp32(pos0 + row) * inv_freq (band_attention.py:43-58).
+ *   lam       fp32 [num_heads / 2] or NULL (lambda = 1).
+ *   out       bf16; query row i (0 <= i < q_count, buffer row q_begin + i) of batch b at
+ *             out + (b * q_count + i) * out_row_stride, pointing at the column of head 2 * pair_begin.
+ *   window    band half-width: query at buffer row r sees keys k with |k - r| <= window, 0 <= k < rows.
+ *   pos0      global sequence position of buffer row 0 (0 unless sequence-sharded).
+ * head_dim must be 64 (band_attention.py:138-140). */
+int hb_band_diff_attn(const void* qkv, int64_t qkv_row_stride, const float* q_norm, const float* k_norm,
+                      const float* inv_freq, int half, const float* lam, void* out, int64_t out_row_stride,
+                      int batch, int rows, int q_begin, int q_count, int64_t pos0, int num_heads, int head_dim,
+                      int window, int pair_begin, int pair_count, void* workspace, size_t workspace_bytes,
+                      cudaStream_t stream);
+
+/* ---- W8A8 int8 GEMM (DiT MLP) ------------------------------------------------------------------------ */
+/* Per-row symmetric int8 quantisation of a bf16 matrix x [rows, K] (leading dim ldx elements):
+ * scale[r] = absmax / 127 (1 for an all-zero row), q = clamp(rint(x / scale), -127, 127).
+ * Used per token on activations and per output channel on weights [N, K]. No reference counterpart:
+ * the reference's MLP is a bf16 `_linear` (dit.py:33-36, 218-221); the scheme is the benchmark's. */
+int hb_quant_rows_int8(const void* x, int64_t ldx, int rows, int K, void* q, int64_t ldq, float* scale,
+                       cudaStream_t stream);
+
+/* y[m, n] = bf16(((float)acc[m, n] * sx[m]) * sw[n] + bias[n]), acc = sum_k qx[m, k] * qw[n, k] in int32.
+ * Replaces `dit._linear(x, W, b)` (dit.py:33-36) at its `_feed_forward` call sites (dit.py:220-221).
+ *   qx  int8 [M, K] (ld ldqx bytes, multiple of 16), sx fp32 [M]; qw int8 [N, K], sw fp32 [N];
+ *   bias bf16 [N] or NULL; out bf16 [M, N] (ld ldo elements);
+ *   acc_out  optional int32 [M, N] copy of the accumulators (ld ldacc), NULL to skip.
+ * N must be a multiple of 32, K a multiple of 16. */
+int hb_w8a8_gemm(const void* qx, int64_t ldqx, const float* sx, const void* qw, int64_t ldqw, const float* sw,
+                 const void* bias, void* out, int64_t ldo, int32_t* acc_out, int64_t ldacc, int M, int N, int K,
+                 cudaStream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* HB_B200_H_ */

@@ -1,0 +1,94 @@
+"""CPU: pin the oracle against golden vectors produced by the reference's own XLA-path code
+(tests/golden/make_golden.py), plus the invariants the survey lists (lambda = 0, identical branches,
+band vs dense, W8A8 integer exactness)."""
+import numpy as np
+import pytest
+
+from conftest import load_golden
+from oracle import band, dense, w8a8
+from oracle.common import bf16_bits_to_f32, check_close
+
+DENSE = ["dense_h4_l200_full", "dense_h2_l130_partial", "dense_h2_l257_sharp"]
+BAND = ["band_w17_l204_partial", "band_w128_l384_full", "band_w17_l136_sharp"]
+
+
+def _band_norms(z):
+    q = {"alpha": z["q_alpha"], "gamma": z["q_gamma"], "beta": z["q_beta"]}
+    k = {"alpha": z["k_alpha"], "gamma": z["k_gamma"], "beta": z["k_beta"]}
+    return q, k
+
+
+@pytest.mark.parametrize("name", DENSE)
+def test_dense_oracle_matches_reference(name):
+    z = load_golden(name)
+    qkv = bf16_bits_to_f32(z["qkv_bits"])
+    args = (qkv, z["q_weight"], z["k_weight"], z["inv_freq"], z["valid"], int(z["heads"]), float(z["eps"]))
+    out = dense.dense_diff_attention(*args)
+    check_close(out, z["out_ref"], max_abs=1e-5, mean_abs=1e-6)
+    a, b = dense.dense_branches(*args)
+    check_close(dense.merge_heads(a), z["branch_a"], max_abs=1e-5, mean_abs=1e-6)
+    check_close(dense.merge_heads(b), z["branch_b"], max_abs=1e-5, mean_abs=1e-6)
+    # lambda: A - lambda * B against the reference's own branches
+    lam = z["lam"]
+    ref = z["branch_a"] - np.repeat(lam, 128)[None, None, :] * z["branch_b"]
+    check_close(dense.dense_diff_attention(*args, lam=lam), ref, max_abs=1e-5, mean_abs=1e-6)
+
+
+@pytest.mark.parametrize("name", BAND)
+def test_band_oracle_matches_reference(name):
+    z = load_golden(name)
+    qkv = bf16_bits_to_f32(z["qkv_bits"])
+    qn, kn = _band_norms(z)
+    args = (qkv, qn, kn, z["inv_freq"], int(z["heads"]), int(z["window"]))
+    check_close(band.band_diff_attention(*args), z["out_ref"], max_abs=1e-5, mean_abs=1e-6)
+    a, b = band.band_branches(*args)
+    check_close(dense.merge_heads(a), z["branch_a"], max_abs=1e-5, mean_abs=1e-6)
+    lam = z["lam"]
+    ref = z["branch_a"] - np.repeat(lam, 128)[None, None, :] * z["branch_b"]
+    check_close(band.band_diff_attention(*args, lam=lam), ref, max_abs=1e-5, mean_abs=1e-6)
+
+
+def test_dense_invariants():
+    z = load_golden("dense_h2_l130_partial")
+    qkv = bf16_bits_to_f32(z["qkv_bits"]).copy()
+    args = (z["q_weight"], z["k_weight"], z["inv_freq"], z["valid"], 2, 1e-6)
+    # lambda = 0 is plain attention on branch A
+    out0 = dense.dense_diff_attention(qkv, *args, lam=np.zeros(1, np.float32))
+    check_close(out0, z["branch_a"], max_abs=1e-5, mean_abs=1e-6)
+    # identical branches with lambda = 1 cancel exactly
+    sec = np.split(qkv, 5, axis=-1)
+    same = np.concatenate([sec[0], sec[1], sec[2], sec[0], sec[1]], -1)
+    assert np.abs(dense.dense_diff_attention(same, *args)).max() == 0.0
+
+
+def test_band_window_covering_everything_is_dense_attention():
+    z = load_golden("band_w17_l136_sharp")
+    qkv = bf16_bits_to_f32(z["qkv_bits"])
+    qn, kn = _band_norms(z)
+    wide = band.band_diff_attention(qkv, qn, kn, z["inv_freq"], 2, window=10_000)
+    a, b = band.band_branches(qkv, qn, kn, z["inv_freq"], 2, window=10_000)
+    q, k, v, qd, kd = dense.split_heads(qkv, 2)
+    cos, sin = dense.rope_cos_sin(qkv.shape[1], z["inv_freq"])
+    full_a = dense.softmax_attend(dense.apply_rope(band.dyt(q, qn), cos, sin),
+                                  dense.apply_rope(band.dyt(k, kn), cos, sin), v)
+    check_close(dense.merge_heads(a), dense.merge_heads(full_a), max_abs=1e-9, mean_abs=1e-10)
+    assert wide.shape == (1, 136, 128)
+
+
+def test_w8a8_oracle_matches_integer_golden():
+    z = load_golden("w8a8_m9_k96_n12")
+    y, acc, qx, sx = w8a8.w8a8_linear(z["x_bits"], z["qw"], z["sw"], z["bias_bits"])
+    assert np.array_equal(qx, z["qx"]) and np.array_equal(sx, z["sx"])
+    assert np.array_equal(acc, z["acc"])
+    assert np.array_equal(y, z["y_bits"])
+    qw, sw = w8a8.quantize_rows(bf16_bits_to_f32(z["w_bits"]))
+    assert np.array_equal(qw, z["qw"]) and np.array_equal(sw, z["sw"])
+
+
+def test_quantize_rounding_rules():
+    x = np.array([[127.0, 2.5, -3.5, 0.5, -0.5, 1.5, 126.5, -127.0],
+                  [0, 0, 0, 0, 0, 0, 0, 0]], np.float32)
+    q, s = w8a8.quantize_rows(x)
+    assert s[0] == 1.0 and s[1] == 1.0
+    assert q[0].tolist() == [127, 2, -4, 0, 0, 2, 126, -127]
+    assert q[1].tolist() == [0] * 8

@@ -1,0 +1,69 @@
+"""GPU parity for the W8A8 path through the C ABI: quantisation, int32 accumulators and the bf16 epilogue are
+all bit-exact against the CPU oracle (oracle/w8a8.py)."""
+import numpy as np
+import pytest
+import torch
+
+from conftest import load_golden
+from gpu_util import bf16_cuda, bits_np
+from oracle import w8a8 as ow
+
+pytestmark = pytest.mark.gpu
+
+
+def test_w8a8_golden_bit_exact(cuda_lib):
+    from hummingbird_b200.w8a8 import quantize_rows, w8a8_gemm
+    z = load_golden("w8a8_m9_k96_n12")
+    # pad N to a multiple of 32 (kernel requirement) with zero weight rows; compare the first 12 columns
+    x = bf16_cuda(z["x_bits"])
+    w = np.zeros((32, 96), np.uint16)
+    w[:12] = z["w_bits"]
+    qx, sx = quantize_rows(x)
+    qw, sw = quantize_rows(bf16_cuda(w))
+    bias = np.zeros(32, np.uint16)
+    bias[:12] = z["bias_bits"]
+    acc = torch.empty(9, 32, dtype=torch.int32, device="cuda")
+    y = w8a8_gemm(qx, sx, qw, sw, bf16_cuda(bias), acc_out=acc)
+    torch.cuda.synchronize()
+    assert np.array_equal(qx.cpu().numpy(), z["qx"])
+    assert np.array_equal(sx.cpu().numpy(), z["sx"])
+    assert np.array_equal(qw.cpu().numpy()[:12], z["qw"])
+    assert np.array_equal(acc.cpu().numpy()[:, :12], z["acc"])
+    assert np.array_equal(bits_np(y)[:, :12], z["y_bits"])
+
+
+@pytest.mark.parametrize("m,k,n", [(2584, 1024, 4096), (2584, 4096, 1024), (200, 272, 96), (1, 16, 32)])
+def test_w8a8_gemm_bit_exact(m, k, n, cuda_lib):
+    from hummingbird_b200.w8a8 import quantize_rows, w8a8_gemm
+    g = torch.Generator(device="cuda").manual_seed(m * 7 + k * 3 + n)
+    x = torch.randn(m, k, device="cuda", generator=g).to(torch.bfloat16)
+    w = (torch.randn(n, k, device="cuda", generator=g) / k ** 0.5).to(torch.bfloat16)
+    bias = (0.02 * torch.randn(n, device="cuda", generator=g)).to(torch.bfloat16)
+    qx, sx = quantize_rows(x)
+    qw, sw = quantize_rows(w)
+    acc = torch.empty(m, n, dtype=torch.int32, device="cuda")
+    y = w8a8_gemm(qx, sx, qw, sw, bias, acc_out=acc)
+    torch.cuda.synchronize()
+    xq_ref, sx_ref = ow.quantize_rows(x.float().cpu().numpy())
+    wq_ref, sw_ref = ow.quantize_rows(w.float().cpu().numpy())
+    assert np.array_equal(qx.cpu().numpy(), xq_ref) and np.array_equal(sx.cpu().numpy(), sx_ref)
+    assert np.array_equal(qw.cpu().numpy(), wq_ref) and np.array_equal(sw.cpu().numpy(), sw_ref)
+    acc_ref = ow.int_matmul(xq_ref, wq_ref)
+    assert np.array_equal(acc.cpu().numpy(), acc_ref)
+    y_ref = ow.epilogue(acc_ref, sx_ref, sw_ref, bits_np(bias))
+    assert np.array_equal(bits_np(y), y_ref)
+
+
+def test_w8a8_linear_pair_config3(cuda_lib):
+    """Config 3: GEMM1 (1024 -> 4096) then GEMM2 (4096 -> 1024) on GEMM1's bf16 output, bit-exact."""
+    from hummingbird_b200.w8a8 import W8A8Linear
+    from hummingbird_b200.workloads import w8a8_inputs
+    w = w8a8_inputs("cuda")
+    l1, l2 = W8A8Linear(w.w1, w.b1), W8A8Linear(w.w2, w.b2)
+    h = l1(w.x)
+    y = l2(h)
+    torch.cuda.synchronize()
+    h_ref, _, _, _ = ow.w8a8_linear(bits_np(w.x), l1.qw.cpu().numpy(), l1.sw.cpu().numpy(), bits_np(w.b1))
+    assert np.array_equal(bits_np(h), h_ref)
+    y_ref, _, _, _ = ow.w8a8_linear(h_ref, l2.qw.cpu().numpy(), l2.sw.cpu().numpy(), bits_np(w.b2))
+    assert np.array_equal(bits_np(y), y_ref)
