@@ -12,6 +12,7 @@ LIB_PATH = Path(__file__).resolve().parent / "libhb_b200.so"
 
 HB_OK, HB_ERR_SHAPE, HB_ERR_ALIGN, HB_ERR_ARCH, HB_ERR_LAUNCH = 0, 1, 2, 3, 4
 HB_ERR_DEVICE, HB_ERR_TIMEOUT, HB_ERR_WORKSPACE, HB_ERR_NCCL, HB_ERR_NULL = 5, 6, 7, 8, 9
+HB_STAGE_PREPARE, HB_STAGE_ATTEND, HB_STAGE_ALL = 1, 2, 3
 _NAMES = {0: "ok", 1: "unsupported shape", 2: "misaligned pointer or stride", 3: "device is not sm_100",
           4: "CUDA launch failed", 5: "device error", 6: "device-side wait timed out", 7: "workspace too small",
           8: "collective failed", 9: "null pointer"}
@@ -25,9 +26,9 @@ SIGNATURES: dict[str, list] = {
     "hb_dense_workspace_bytes": [_i, _i, _i, C.POINTER(_sz)],
     "hb_dense_diff_attn": [_p, _i64, _p, _p, _p, _p, _i64, _p, _i64, _i64, _p, _p, _i64, _i, _i, _i, _i, _i, _f,
                            _i, _i, _p, _sz, _p],
-    "hb_band_workspace_bytes": [_i, _i, _i, C.POINTER(_sz)],
+    "hb_band_workspace_bytes": [_i, _i, _i, _i, _i, C.POINTER(_sz)],
     "hb_band_diff_attn": [_p, _i64, _p, _p, _p, _i, _p, _p, _i64, _i, _i, _i, _i, _i64, _i, _i, _i, _i, _i, _p, _sz,
-                          _p],
+                          _i, _p],
     "hb_quant_rows_int8": [_p, _i64, _i, _i, _p, _i64, _p, _p],
     "hb_w8a8_gemm": [_p, _i64, _p, _p, _i64, _p, _p, _p, _i64, _p, _i64, _i, _i, _i, _p],
 }

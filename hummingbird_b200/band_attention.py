@@ -28,19 +28,21 @@ def pack_norm(norm: dict, device: torch.device) -> torch.Tensor:
     return torch.cat([alpha, gamma, beta]).contiguous()
 
 
-def workspace_bytes(batch: int, rows: int, pair_count: int) -> int:
+def workspace_bytes(batch: int, rows: int, pair_count: int, window: int, half: int) -> int:
     n = ctypes.c_size_t(0)
-    _lib.call("hb_band_workspace_bytes", batch, rows, pair_count, ctypes.byref(n))
+    _lib.call("hb_band_workspace_bytes", batch, rows, pair_count, window, half, ctypes.byref(n))
     return int(n.value)
 
 
 def band_attention_shard(qkv: torch.Tensor, q_norm, k_norm, inv_freq: torch.Tensor, num_heads: int,
                          head_dim: int, window: int, *, q_begin: int, q_count: int, pos0: int,
                          lam: torch.Tensor | None = None, pair_begin: int = 0, pair_count: int | None = None,
-                         out: torch.Tensor | None = None, ws: torch.Tensor | None = None) -> torch.Tensor:
+                         out: torch.Tensor | None = None, ws: torch.Tensor | None = None,
+                         stages: int = _lib.HB_STAGE_ALL) -> torch.Tensor:
     """Band attention over a buffer of `rows` consecutive sequence rows (a shard plus its halos):
     queries are buffer rows `[q_begin, q_begin + q_count)`, every buffer row is a key, and buffer row 0 sits
-    at global position `pos0`. Returns `(B, q_count, 2 * pair_count * 64)` bf16."""
+    at global position `pos0`. Returns `(B, q_count, 2 * pair_count * 64)` bf16. `stages` may issue only the
+    preparation (HB_STAGE_PREPARE) or only the attention (HB_STAGE_ATTEND) half, on the same `ws`."""
     if head_dim != 64:
         raise ValueError(f"band_attention: need head_dim 64 (head_dim={head_dim})")
     if qkv.dim() != 3 or qkv.dtype != torch.bfloat16 or qkv.shape[-1] != 5 * num_heads * head_dim:
@@ -56,11 +58,11 @@ def band_attention_shard(qkv: torch.Tensor, q_norm, k_norm, inv_freq: torch.Tens
         lam = lam.to(device=qkv.device, dtype=torch.float32).contiguous()
     if out is None:
         out = torch.empty(batch, q_count, 2 * pair_count * head_dim, dtype=torch.bfloat16, device=qkv.device)
-    need = workspace_bytes(batch, rows, pair_count)
+    need = workspace_bytes(batch, rows, pair_count, window, freqs.shape[0])
     ws = workspace(need, qkv.device) if ws is None else ws
     _lib.call("hb_band_diff_attn", ptr(qkv), qkv.stride(1), ptr(qn), ptr(kn), ptr(freqs), freqs.shape[0], ptr(lam),
               ptr(out), out.stride(1), batch, rows, q_begin, q_count, pos0, num_heads, head_dim, window, pair_begin,
-              pair_count, ptr(ws), ws.numel(), stream_handle(qkv.device))
+              pair_count, ptr(ws), ws.numel(), stages, stream_handle(qkv.device))
     return out
 
 

@@ -301,8 +301,10 @@ __global__ void __launch_bounds__(kThreads, 1) diff_attention_kernel(const AttnP
           uint32_t w[16];
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
-            const float y0 = __uint_as_float(oa[2 * j]) * inv_a - __uint_as_float(ob[2 * j]) * sb;
-            const float y1 = __uint_as_float(oa[2 * j + 1]) * inv_a - __uint_as_float(ob[2 * j + 1]) * sb;
+            // each branch normalised and rounded on its own, then one fp32 subtraction (no contraction)
+            const float y0 = __fmul_rn(__uint_as_float(oa[2 * j]), inv_a) - __fmul_rn(__uint_as_float(ob[2 * j]), sb);
+            const float y1 =
+                __fmul_rn(__uint_as_float(oa[2 * j + 1]), inv_a) - __fmul_rn(__uint_as_float(ob[2 * j + 1]), sb);
             w[j] = pack_bf16x2(y0, y1);
           }
           uint4* d4 = reinterpret_cast<uint4*>(dst + 32 * c);

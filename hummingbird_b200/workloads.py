@@ -30,8 +30,8 @@ def _project(x: np.ndarray, w: np.ndarray, device) -> torch.Tensor:
     prev = torch.backends.cuda.matmul.allow_tf32
     torch.backends.cuda.matmul.allow_tf32 = False
     try:
-        xt = torch.from_numpy(x).to(device)
-        wt = torch.from_numpy(w).to(device)
+        xt = torch.from_numpy(np.asarray(x, np.float32)).to(device)
+        wt = torch.from_numpy(np.asarray(w, np.float32)).to(device)
         return (xt @ wt.T).to(torch.bfloat16)
     finally:
         torch.backends.cuda.matmul.allow_tf32 = prev
@@ -76,9 +76,12 @@ class BandInputs:
     window: int
 
 
-def band_inputs(device, *, seed=1, batch=1, length=82_688, d_model=512, heads=8, half=16, window=128):
+def band_inputs(device, *, seed=1, batch=1, length=82_688, d_model=512, heads=8, half=16, window=128, x_seed=None):
+    """`x_seed` (e.g. `(1, rank)`) draws other rows of the same sequence with the same weights."""
     rng = np.random.default_rng(seed)
     x = rng.standard_normal((batch * length, d_model), dtype=np.float32)
+    if x_seed is not None:
+        x = np.random.default_rng(x_seed).standard_normal((batch * length, d_model), dtype=np.float32)
     w = np.concatenate([rng.standard_normal((heads * 64, d_model), dtype=np.float32) / np.sqrt(d_model)
                         for _ in range(5)])
 

@@ -62,8 +62,17 @@ int hb_dense_diff_attn(const void* qkv, int64_t qkv_row_stride, const float* q_w
                        cudaStream_t stream);
 
 /* ---- band (sliding-window) differential attention (SAME-L decoder) --------------------------------- */
-/* Bytes of workspace hb_band_diff_attn needs for `rows` buffer rows and `pair_count` head pairs. */
-int hb_band_workspace_bytes(int batch, int rows, int pair_count, size_t* bytes);
+/* Bytes of workspace hb_band_diff_attn needs for `rows` buffer rows, `pair_count` head pairs, `window` and
+ * rotate-half width `half`: a rows x half (cos, sin) table for window <= 128 (the fused kernel), prepared
+ * operand tiles otherwise. */
+int hb_band_workspace_bytes(int batch, int rows, int pair_count, int window, int half, size_t* bytes);
+
+/* Stage selector of hb_band_diff_attn: the call is a prologue kernel that prepares DyT/RoPE'd operand
+ * tiles in the workspace, then the attention kernel that consumes them. HB_STAGE_ALL runs both; the two
+ * halves can be issued separately (same arguments, same workspace) to overlap other work between them. */
+#define HB_STAGE_PREPARE 1
+#define HB_STAGE_ATTEND 2
+#define HB_STAGE_ALL 3
 
 /* Replaces `sa3jax.band_attention.band_attention(qkv, q_norm, k_norm, inv_freq, num_heads, head_dim,
  * window)` (band_attention.py:123-180), the kernel `same_l._attention` calls under
@@ -82,7 +91,7 @@ int hb_band_diff_attn(const void* qkv, int64_t qkv_row_stride, const float* q_no
                       const float* inv_freq, int half, const float* lam, void* out, int64_t out_row_stride,
                       int batch, int rows, int q_begin, int q_count, int64_t pos0, int num_heads, int head_dim,
                       int window, int pair_begin, int pair_count, void* workspace, size_t workspace_bytes,
-                      cudaStream_t stream);
+                      int stages, cudaStream_t stream);
 
 /* ---- W8A8 int8 GEMM (DiT MLP) ------------------------------------------------------------------------ */
 /* Per-row symmetric int8 quantisation of a bf16 matrix x [rows, K] (leading dim ldx elements):

@@ -22,9 +22,8 @@ from oracle.dense import HEAD_DIM, apply_rope, bf16, merge_heads, rope_cos_sin, 
 
 def dyt(x: np.ndarray, norm: dict) -> np.ndarray:
     """`DynamicTanh`: `gamma * tanh(alpha * x) + beta`, alpha a scalar (same_l.py:58-69)."""
-    alpha = float(np.asarray(norm["alpha"], np.float32).reshape(-1)[0])
-    return (np.asarray(norm["gamma"], np.float64) * np.tanh(alpha * x)
-            + np.asarray(norm["beta"], np.float64))
+    alpha = x.dtype.type(np.asarray(norm["alpha"], np.float32).reshape(-1)[0])
+    return (np.asarray(norm["gamma"], x.dtype) * np.tanh(alpha * x) + np.asarray(norm["beta"], x.dtype))
 
 
 def band_attend(q: np.ndarray, k: np.ndarray, v: np.ndarray, window: int, block: int = 256,
@@ -32,7 +31,7 @@ def band_attend(q: np.ndarray, k: np.ndarray, v: np.ndarray, window: int, block:
     """Band softmax attention `(B, H, L, 64)`: query i sees keys j with `|j - i| <= window`, `0 <= j < L`."""
     b, h, length, d = q.shape
     out = np.empty_like(q)
-    scale = 1.0 / np.sqrt(HEAD_DIM)
+    scale = q.dtype.type(1.0 / np.sqrt(HEAD_DIM))
     for q0 in range(0, length, block):
         q1 = min(length, q0 + block)
         k0, k1 = max(0, q0 - window), min(length, q1 + window)
@@ -52,14 +51,15 @@ def band_attend(q: np.ndarray, k: np.ndarray, v: np.ndarray, window: int, block:
 
 
 def band_branches(qkv: np.ndarray, q_norm: dict, k_norm: dict, freqs: np.ndarray, num_heads: int,
-                  window: int, offset: int = 0, fused_casts: bool = False) -> tuple[np.ndarray, np.ndarray]:
+                  window: int, offset: int = 0, fused_casts: bool = False,
+                  dtype=np.float64) -> tuple[np.ndarray, np.ndarray]:
     """Branches A and B `(B, H, L, 64)`; `offset` is the sequence position of row 0 (for a slice).
 
     `fused_casts=True` adds the reference fused kernel's cast points (band_attention.py:82-85, 96-101):
     DyT + RoPE output -> bf16, bf16 softmax weights into `P @ V`, normalised after."""
-    q, k, v, qd, kd = split_heads(qkv, num_heads)
+    q, k, v, qd, kd = split_heads(qkv, num_heads, dtype=dtype)
     length = qkv.shape[1]
-    cos, sin = rope_cos_sin(length, freqs, offset)
+    cos, sin = rope_cos_sin(length, freqs, offset, dtype)
     cast = bf16 if fused_casts else (lambda t: t)
     q, qd = (cast(apply_rope(dyt(t, q_norm), cos, sin)) for t in (q, qd))
     k, kd = (cast(apply_rope(dyt(t, k_norm), cos, sin)) for t in (k, kd))
@@ -69,8 +69,8 @@ def band_branches(qkv: np.ndarray, q_norm: dict, k_norm: dict, freqs: np.ndarray
 
 def band_diff_attention(qkv: np.ndarray, q_norm: dict, k_norm: dict, freqs: np.ndarray, num_heads: int,
                         window: int, lam: np.ndarray | None = None, offset: int = 0,
-                        fused_casts: bool = False) -> np.ndarray:
+                        fused_casts: bool = False, dtype=np.float64) -> np.ndarray:
     """`(B, L, 5 * H * 64)` -> `(B, L, H * 64)` fp32: `A - lambda[pair] * B` per head (pair = head // 2)."""
-    a, b = band_branches(qkv, q_norm, k_norm, freqs, num_heads, window, offset, fused_casts)
-    lam_h = np.ones(num_heads) if lam is None else np.repeat(np.asarray(lam, np.float64), 2)
+    a, b = band_branches(qkv, q_norm, k_norm, freqs, num_heads, window, offset, fused_casts, dtype)
+    lam_h = np.ones(num_heads, dtype) if lam is None else np.repeat(np.asarray(lam, dtype), 2)
     return merge_heads(a - lam_h[None, :, None, None] * b).astype(np.float32)

@@ -1,0 +1,134 @@
+"""Timed CPU baselines: the oracle port run on the host's cores — test / benchmark infrastructure only.
+
+Used by `bench.py` (`cpu_baseline` and `--impl reference`): the reference's own XLA CPU path cannot run here
+(JAX is not installed), so its fp32 restatement in `oracle.band` / `oracle.dense` / `oracle.w8a8` stands in
+for it, computed in float32 (the reference's FP32 XLA precision) and spread over the host's cores with a
+`spawn` process pool (one BLAS thread per worker), on a bounded sample of the benchmark's workload.
+"""
+from __future__ import annotations
+
+import multiprocessing as mp
+import os
+import time
+
+import numpy as np
+
+_POOL = None
+_WORKERS = 0
+
+
+def _init_worker():
+    """One BLAS thread per worker process (the pool supplies the parallelism)."""
+    from threadpoolctl import threadpool_limits
+    threadpool_limits(1)
+
+
+def pool(workers: int | None = None):
+    """A spawn-context pool (safe to create after CUDA initialisation in the parent)."""
+    global _POOL, _WORKERS
+    workers = workers or os.cpu_count() or 1
+    if _POOL is None or _WORKERS != workers:
+        ctx = mp.get_context("spawn")
+        saved = {k: os.environ.get(k) for k in ("OMP_NUM_THREADS", "OPENBLAS_NUM_THREADS", "MKL_NUM_THREADS")}
+        os.environ.update({k: "1" for k in saved})  # inherited by the spawned workers before numpy loads
+        try:
+            _POOL = ctx.Pool(workers, initializer=_init_worker)
+        finally:
+            for k, v in saved.items():
+                if v is None:
+                    os.environ.pop(k, None)
+                else:
+                    os.environ[k] = v
+        _WORKERS = workers
+    return _POOL
+
+
+def shutdown():
+    global _POOL
+    if _POOL is not None:
+        _POOL.terminate()
+        _POOL = None
+
+
+def band_flops(length: int, heads: int, window: int, q0: int = 0, q1: int | None = None) -> float:
+    """Algorithmic FLOPs of band differential attention over queries [q0, q1): 2 branches x (QK^T + PV) x
+    2 FLOP x 64 dims x heads x sum_q |{k : |k - q| <= window, 0 <= k < length}|."""
+    q1 = length if q1 is None else q1
+    q = np.arange(q0, q1, dtype=np.int64)
+    keys = np.minimum(length - 1, q + window) - np.maximum(0, q - window) + 1
+    return float(2 * 2 * 2 * 64 * heads * keys.sum())
+
+
+def dense_flops(batch: int, length: int, heads: int) -> float:
+    """2 branches x (QK^T + PV) x 2 FLOP x 64 x L^2 per head: 8 * B * H * L^2 * 64."""
+    return 8.0 * batch * heads * length * length * 64
+
+
+_SHM_CACHE: dict = {}
+
+
+def _attach(name: str, shape: tuple) -> np.ndarray:
+    from multiprocessing import shared_memory
+    if name not in _SHM_CACHE:
+        _SHM_CACHE.clear()
+        shm = shared_memory.SharedMemory(name=name)
+        _SHM_CACHE[name] = (shm, np.ndarray(shape, np.float32, buffer=shm.buf))
+    return _SHM_CACHE[name][1]
+
+
+def _band_task(args):
+    from oracle.band import band_diff_attention
+    name, shape, qn, kn, freqs, heads, window, lam, lo, hi, q0, q1 = args
+    qkv = _attach(name, shape)[:, lo:hi]
+    out = band_diff_attention(qkv, qn, kn, freqs, heads, window, lam=lam, offset=lo, dtype=np.float32)
+    return float(out[:, q0 - lo:q1 - lo].sum())
+
+
+def time_band_sample(qkv: np.ndarray, q_norm: dict, k_norm: dict, freqs: np.ndarray, heads: int, window: int,
+                     lam: np.ndarray, q_rows: int, workers: int | None = None, chunk: int = 256) -> dict:
+    """Time the oracle on queries [0, q_rows) of `qkv` (float32 `(1, L, 5 H 64)`, placed in shared memory),
+    split into `chunk`-row tasks (each reading its +-window halo) over a spawn pool. Returns seconds, FLOPs
+    and the worker count."""
+    from multiprocessing import shared_memory
+    length = qkv.shape[1]
+    p = pool(workers)
+    shm = shared_memory.SharedMemory(create=True, size=qkv.nbytes)
+    try:
+        np.ndarray(qkv.shape, np.float32, buffer=shm.buf)[...] = qkv
+        tasks = []
+        for q0 in range(0, q_rows, chunk):
+            q1 = min(q_rows, q0 + chunk)
+            lo, hi = max(0, q0 - window), min(length, q1 + window)
+            tasks.append((shm.name, qkv.shape, q_norm, k_norm, freqs, heads, window, lam, lo, hi, q0, q1))
+        p.map(_band_task, tasks[: min(len(tasks), _WORKERS)])  # warm the workers (imports, BLAS, mapping)
+        t0 = time.perf_counter()
+        p.map(_band_task, tasks)
+        seconds = time.perf_counter() - t0
+    finally:
+        shm.close()
+        shm.unlink()
+    return {"seconds": seconds, "flops": band_flops(length, heads, window, 0, q_rows), "cores": _WORKERS}
+
+
+def _dense_task(args):
+    from oracle.dense import dense_branches
+    qkv, q_w, k_w, freqs, valid, heads, eps = args
+    a, b = dense_branches(qkv.astype(np.float32), q_w, k_w, freqs, valid, heads, eps)
+    return a.shape
+
+
+def time_dense_sample(qkv: np.ndarray, q_w, k_w, freqs, valid, heads: int, eps: float,
+                      workers: int | None = None) -> dict:
+    """Time the dense oracle over all heads of `qkv`, one task per head."""
+    p = pool(workers)
+    b, length, _ = qkv.shape
+    sec = np.split(qkv, 5, axis=-1)
+    tasks = []
+    for h in range(heads):
+        cols = [s[..., h * 64:(h + 1) * 64] for s in sec]
+        tasks.append((np.concatenate(cols, -1), q_w, k_w, freqs, valid, 1, eps))
+    p.map(_dense_task, tasks[: min(len(tasks), _WORKERS)])
+    t0 = time.perf_counter()
+    p.map(_dense_task, tasks)
+    seconds = time.perf_counter() - t0
+    return {"seconds": seconds, "flops": dense_flops(b, length, heads), "cores": _WORKERS}

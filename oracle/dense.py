@@ -30,11 +30,12 @@ def rope_angles(length: int, freqs: np.ndarray, offset: int = 0) -> np.ndarray:
     return pos[:, None] * np.asarray(freqs, np.float32)[None, :]
 
 
-def rope_cos_sin(length: int, freqs: np.ndarray, offset: int = 0) -> tuple[np.ndarray, np.ndarray]:
-    """`(L, 2 * half)` cos / sin as float64 of the fp32 angles (`cat(freqs, freqs)`)."""
+def rope_cos_sin(length: int, freqs: np.ndarray, offset: int = 0,
+                 dtype=np.float64) -> tuple[np.ndarray, np.ndarray]:
+    """`(L, 2 * half)` cos / sin of the fp32 angles (`cat(freqs, freqs)`), evaluated in float64."""
     ang = rope_angles(length, freqs, offset).astype(np.float64)
     ang = np.concatenate([ang, ang], axis=-1)
-    return np.cos(ang), np.sin(ang)
+    return np.cos(ang).astype(dtype), np.sin(ang).astype(dtype)
 
 
 def apply_rope(x: np.ndarray, cos: np.ndarray, sin: np.ndarray) -> np.ndarray:
@@ -51,10 +52,11 @@ def rms_norm(x: np.ndarray, weight: np.ndarray, eps: float) -> np.ndarray:
     return x / np.sqrt(ms + eps) * np.asarray(weight, np.float64)
 
 
-def split_heads(qkv: np.ndarray, num_heads: int, sections: int = 5) -> list[np.ndarray]:
-    """`(B, L, sections * H * 64)` -> `sections` arrays `(B, H, L, 64)` in float64."""
+def split_heads(qkv: np.ndarray, num_heads: int, sections: int = 5, dtype=np.float64) -> list[np.ndarray]:
+    """`(B, L, sections * H * 64)` -> `sections` arrays `(B, H, L, 64)` (float64 unless `dtype` says otherwise:
+    the timed CPU baseline runs in float32, the precision of the reference's FP32 XLA path)."""
     b, length, _ = qkv.shape
-    parts = np.split(np.asarray(qkv, np.float64), sections, axis=-1)
+    parts = np.split(np.asarray(qkv, dtype), sections, axis=-1)
     return [p.reshape(b, length, num_heads, HEAD_DIM).transpose(0, 2, 1, 3) for p in parts]
 
 
