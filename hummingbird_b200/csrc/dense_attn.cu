@@ -7,6 +7,8 @@
 //   v:                    bf16(v * mask)                                   (dense_attention.py:77)
 // The 1/sqrt(64) score scale is applied in the softmax (exact: a power of two).
 // Main kernel: attn_kernel.cu (dense mode: every key, no key mask, dense_attention.py:79-83).
+#include <atomic>
+
 #include <cuda_runtime.h>
 
 #include "../../include/hb_b200.h"
@@ -156,4 +158,60 @@ extern "C" int hb_dense_diff_attn(const void* qkv, int64_t qkv_row_stride, const
   ap.out = static_cast<uint16_t*>(out);
   ap.out_row_stride = out_row_stride;
   return launch_diff_attention(ap, stream) == cudaSuccess ? HB_OK : HB_ERR_LAUNCH;
+}
+
+// ------------------------------------------------------------------------------------------------------
+// Allocation-free variant of hb_dense_diff_attn.
+//
+// Some callers cannot hand this library a workspace: an XLA FFI handler runs inside a runtime that has
+// already reserved most of the GPU's memory for its own allocator (JAX pre-allocates about three quarters
+// of it), so a cudaMalloc from the handler can fail, and cudaMalloc / cudaFree also synchronise the device
+// in the middle of the caller's stream work. For them the prepared-tile scratch lives in one fixed array
+// compiled into this library. Its size is a hard limit on the shapes this entry point accepts.
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = 64ull << 20;  // 64 MiB per device that loads the library, held until exit
+
+// Device-side scratch shared by every call of hb_dense_diff_attn_noalloc on a device. Host code must not
+// pass this symbol to a kernel: on the host it only names a stand-in, not the device address.
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+
+// Device address of g_noalloc_scratch on the current device, looked up once per device.
+int noalloc_scratch_address(void** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return HB_ERR_LAUNCH;
+  static std::atomic<void*> cache[64];
+  void* ptr = cache[dev].load(std::memory_order_acquire);
+  if (!ptr) {
+    if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || !ptr) return HB_ERR_LAUNCH;
+    cache[dev].store(ptr, std::memory_order_release);
+  }
+  *out = ptr;
+  return HB_OK;
+}
+
+}  // namespace
+
+extern "C" int hb_dense_noalloc_max_bytes(size_t* bytes) {
+  if (!bytes) return HB_ERR_NULL;
+  *bytes = kNoAllocScratchBytes;
+  return HB_OK;
+}
+
+extern "C" int hb_dense_diff_attn_noalloc(const void* qkv, int64_t qkv_row_stride, const float* q_weight,
+                                          const float* k_weight, const float* cos, const float* sin,
+                                          int64_t table_stride, const void* vmask, int64_t mask_batch_stride,
+                                          int64_t mask_row_stride, const float* lam, void* out,
+                                          int64_t out_row_stride, int batch, int length, int num_heads,
+                                          int head_dim, int half, float eps, int pair_begin, int pair_count,
+                                          cudaStream_t stream) {
+  if (batch < 1 || length < 1 || pair_count < 1) return HB_ERR_SHAPE;
+  // refuse, before any device work, a problem whose prepared tiles would not fit the fixed scratch
+  if (prep_workspace_bytes(batch, length, 2 * pair_count) > kNoAllocScratchBytes) return HB_ERR_WORKSPACE;
+  void* scratch = nullptr;
+  const int st = noalloc_scratch_address(&scratch);
+  if (st != HB_OK) return st;
+  return hb_dense_diff_attn(qkv, qkv_row_stride, q_weight, k_weight, cos, sin, table_stride, vmask, mask_batch_stride,
+                            mask_row_stride, lam, out, out_row_stride, batch, length, num_heads, head_dim, half, eps,
+                            pair_begin, pair_count, scratch, kNoAllocScratchBytes, stream);
 }

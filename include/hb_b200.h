@@ -61,6 +61,26 @@ int hb_dense_diff_attn(const void* qkv, int64_t qkv_row_stride, const float* q_w
                        float eps, int pair_begin, int pair_count, void* workspace, size_t workspace_bytes,
                        cudaStream_t stream);
 
+/* Allocation-free form of hb_dense_diff_attn, for callers that cannot allocate device memory or pass a
+ * workspace (e.g. a handler inside a runtime that has reserved most of the GPU's memory for its own
+ * allocator, or code that must not let cudaMalloc / cudaFree synchronise the device mid-stream). No
+ * counterpart exists in the reference. Same arguments and results as hb_dense_diff_attn without the
+ * workspace: the prepared tiles go to one scratch array of hb_dense_noalloc_max_bytes (64 MiB) built into
+ * the library, which every device that loads the library holds until the process exits.
+ *   - Problems whose workspace (hb_dense_workspace_bytes) exceeds that size return HB_ERR_WORKSPACE before
+ *     anything is launched (e.g. B=1, L=1,422, 24 heads needs 22.5 MiB; B=2, L=2,648, 16 heads 53.8 MiB).
+ *   - The first call on a device looks up the scratch's device address (once per device, with that device
+ *     current); make that first call before capturing a stream.
+ *   - All calls on a device share the one scratch array and it keeps the previous call's contents (each call
+ *     rewrites every byte it reads, so nothing needs clearing): calls that may overlap on the GPU (other
+ *     streams, other host threads) race on it and must be serialised by the caller. */
+int hb_dense_noalloc_max_bytes(size_t* bytes);
+int hb_dense_diff_attn_noalloc(const void* qkv, int64_t qkv_row_stride, const float* q_weight, const float* k_weight,
+                               const float* cos, const float* sin, int64_t table_stride, const void* vmask,
+                               int64_t mask_batch_stride, int64_t mask_row_stride, const float* lam, void* out,
+                               int64_t out_row_stride, int batch, int length, int num_heads, int head_dim, int half,
+                               float eps, int pair_begin, int pair_count, cudaStream_t stream);
+
 /* ---- band (sliding-window) differential attention (SAME-L decoder) --------------------------------- */
 /* Bytes of workspace hb_band_diff_attn needs for `rows` buffer rows, `pair_count` head pairs, `window` and
  * rotate-half width `half`: a rows x half (cos, sin) table for window <= 128 (the fused kernel), prepared
