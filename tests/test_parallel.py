@@ -1,0 +1,85 @@
+"""CPU (gloo, world_size 2 and 3): the host-side partitioning of the multi-GPU paths — row / pair / clip
+shards, the halo exchange that feeds sequence-sharded band attention, and the head-pair all-gather."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from hummingbird_b200 import parallel as par
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _run(fn, world, *args):
+    port = _free_port()
+    mp.spawn(_entry, args=(fn, world, port, args), nprocs=world, join=True)
+
+
+def _entry(rank, fn, world, port, args):
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    try:
+        fn(rank, world, *args)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_row_shards_cover_sequence_with_aligned_boundaries():
+    for length in (82_688, 1000, 261_888):
+        for world in (1, 2, 3, 8):
+            bounds = [par.shard_rows(length, world, r) for r in range(world)]
+            assert bounds[0][0] == 0 and bounds[-1][1] == length
+            for (a0, a1), (b0, b1) in zip(bounds, bounds[1:]):
+                assert a1 == b0 and a1 % 128 == 0
+
+
+def test_pair_shards_cover_pairs_including_uneven_split():
+    for pairs, world in ((8, 2), (8, 8), (12, 8), (4, 4)):
+        sh = [par.shard_pairs(pairs, world, r) for r in range(world)]
+        assert sh[0][0] == 0 and sh[-1][1] == pairs
+        sizes = [b - a for a, b in sh]
+        assert max(sizes) - min(sizes) <= 1
+
+
+def test_qkv_columns_select_pair_lanes_of_every_section():
+    cols = par.qkv_columns_for_pairs(heads=16, p0=2, p1=4)
+    assert cols.numel() == 5 * 2 * 128
+    assert cols[0].item() == 256 and cols[256].item() == 1024 + 256
+
+
+def _halo_worker(rank, world, length, window):
+    lay = par.band_layout(length, world, rank, window)
+    rows = torch.arange(length, dtype=torch.float32)[None, :, None].repeat(1, 1, 4)  # row index as value
+    buf = torch.full((1, lay["rows"], 4), -1.0)
+    buf[:, lay["before"]:lay["before"] + lay["q_count"]] = rows[:, lay["s0"]:lay["s1"]]
+    par.halo_exchange(buf, lay, rank)
+    expect = rows[:, lay["pos0"]:lay["pos0"] + lay["rows"]]
+    assert torch.equal(buf, expect), f"rank {rank}: halo rows differ"
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_halo_exchange_gloo(world):
+    _run(_halo_worker, world, 1000, 128)
+
+
+def _gather_worker(rank, world, pairs):
+    p0, p1 = par.shard_pairs(pairs, world, rank)
+    local = torch.arange(p0 * 128, p1 * 128, dtype=torch.float32).repeat(2, 3, 1)
+    full = par.gather_pairs(local, pairs, world)
+    assert torch.equal(full, torch.arange(pairs * 128, dtype=torch.float32).repeat(2, 3, 1))
+
+
+@pytest.mark.parametrize("world,pairs", [(2, 8), (3, 8)])
+def test_gather_pairs_gloo(world, pairs):
+    _run(_gather_worker, world, pairs)
+
+
+def test_shard_shorter_than_window_is_rejected():
+    with pytest.raises(ValueError):
+        par.band_layout(300, 3, 2, 128)  # the last shard holds rows 256..300
