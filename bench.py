@@ -36,7 +36,7 @@ WINDOW = 128
 L_PER_GPU = 82_688
 HEADS = 8
 # DRAM bytes per launch of band_fused_kernel on this workload, from the committed ncu capture (None until taken)
-BAND_NCU_TRAFFIC = None
+BAND_NCU_TRAFFIC = 509_725_952
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 
@@ -457,8 +457,8 @@ def main():
         "gpu_launches": step.launches * args.steps,
         "roofline": {"bound": "hbm", "kernel": "band_fused_kernel", "achieved": achieved, "peak": peaks["hbm_gbs"],
                      "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"], "traffic": BAND_NCU_TRAFFIC,
-                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch of this "
-                                       "workload (profiles/band_fused_kernel_config2.md)",
+                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch of "
+                                       "this workload (committed summary under profiles/)",
                      "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs, burst copy)" if peak_kind == "measured"
                      else "fallback 6650 GB/s", "algorithmic_bytes_per_launch": k_bytes, "kernel_ms": k_ms,
                      "tensor_frac_of_bf16": value / world / peaks["bf16_tflops"],
