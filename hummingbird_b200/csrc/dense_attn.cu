@@ -1,6 +1,7 @@
 // Dense differential self-attention (the DiT's `dense_attention`), C-ABI front end + its prologue.
 //
-// Prologue (`dense_prep_kernel`, HBM-bound): reads the `to_qkv` output once with 128-bit loads and writes
+// Prologue (`dense_prep_kernel`, HBM-bound): reads the `to_qkv` output once with 128-bit loads (several per
+// thread in flight) and writes
 // per-(batch, head, section) 128-row tiles in the SW128 UMMA image:
 //   q, k, q_diff, k_diff: RMSNorm in fp32 over the head's 64 dims -> bf16 -> RoPE in fp32 with the
 //                         caller's cos / signed-sin lane tables -> bf16   (dense_attention.py:61-69)
@@ -19,8 +20,8 @@
 namespace hb {
 namespace {
 
-constexpr int kPrepRows = 16;
 constexpr int kPrepThreads = 256;
+constexpr int kUnitsPerGroup = 4;  // units (one row x one section x one head) per 8-thread group, loads issued together
 
 struct DensePrepParams {
   const uint16_t* qkv;
@@ -37,28 +38,48 @@ struct DensePrepParams {
   int half;
   uint8_t* ws;
   int ntiles;
+  int units;  // B * ntiles * 128 * 5 * heads (< 2^31, checked on the host)
 };
 
+// Unit u = ((b * rows_pad + row) * 5 + section) * heads + head: consecutive 8-thread groups take consecutive
+// units (consecutive 128-byte pieces of a qkv row), and each group takes kUnitsPerGroup units spaced a grid
+// apart, loading all of them before computing.
 __global__ void __launch_bounds__(kPrepThreads) dense_prep_kernel(const DensePrepParams p) {
-  const int b = blockIdx.y;
-  const int row0 = blockIdx.x * kPrepRows;
   const int lane = threadIdx.x & 31;
-  const int g = threadIdx.x >> 3, c = threadIdx.x & 7;
+  const int c = threadIdx.x & 7;
   const unsigned gmask = 0xFFu << (lane & 24);
-  const int per_row = kSections * p.heads;
-  const int total = kPrepRows * per_row;
   const int hc8 = p.half >> 3;
-  for (int u = g; u < total; u += kPrepThreads / 8) {
-    const int rr = u / per_row, rem = u - rr * per_row;
-    const int s = rem / p.heads, hl = rem - s * p.heads;
-    const int row = row0 + rr;
+  const int group = blockIdx.x * (kPrepThreads / 8) + (threadIdx.x >> 3);
+  const int stride = gridDim.x * (kPrepThreads / 8);
+  const int rows_pad = p.ntiles * kTileRows;
+  uint4 raw[kUnitsPerGroup];
+#pragma unroll
+  for (int k = 0; k < kUnitsPerGroup; ++k) {
+    const int u = group + k * stride;
+    raw[k] = make_uint4(0, 0, 0, 0);
+    if (u < p.units) {
+      const int hl = u % p.heads;
+      const int rs = u / p.heads;
+      const int s = rs % kSections;
+      const int br = rs / kSections;
+      const int row = br % rows_pad, b = br / rows_pad;
+      if (row < p.L)
+        raw[k] = ld_nc_v4(p.qkv + ((size_t)b * p.L + row) * p.qkv_row_stride + (size_t)s * p.H_total * kHeadDim +
+                          (size_t)(p.head0 + hl) * kHeadDim + c * 8);
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < kUnitsPerGroup; ++k) {
+    const int u = group + k * stride;
+    if (u >= p.units) break;  // uniform within the 8-thread group (same u)
+    const int hl = u % p.heads;
+    const int rs = u / p.heads;
+    const int s = rs % kSections;
+    const int br = rs / kSections;
+    const int row = br % rows_pad, b = br / rows_pad;
     const bool valid = row < p.L;
-    uint4 raw = make_uint4(0, 0, 0, 0);
-    if (valid)
-      raw = ld_nc_v4(p.qkv + ((size_t)b * p.L + row) * p.qkv_row_stride + (size_t)s * p.H_total * kHeadDim +
-                     (size_t)(p.head0 + hl) * kHeadDim + c * 8);
     float x[8];
-    unpack8(raw, x);
+    unpack8(raw[k], x);
     uint4 outv;
     if (s == 2) {
       const float m = valid ? __uint_as_float((uint32_t)p.vmask[b * p.mask_bstride + row * p.mask_lstride] << 16) : 0.f;
@@ -137,11 +158,14 @@ extern "C" int hb_dense_diff_attn(const void* qkv, int64_t qkv_row_stride, const
   if (st != HB_OK) return st;
 
   const int ntiles = (length + kTileRows - 1) / kTileRows;
+  const int64_t units = (int64_t)batch * ntiles * kTileRows * kSections * heads;
+  if (units >= (int64_t(1) << 31)) return HB_ERR_SHAPE;
   DensePrepParams pp{static_cast<const uint16_t*>(qkv), qkv_row_stride, batch, length, num_heads, 2 * pair_begin,
                      heads, q_weight, k_weight, cos, sin, table_stride, static_cast<const uint16_t*>(vmask),
-                     mask_batch_stride, mask_row_stride, eps, half, static_cast<uint8_t*>(workspace), ntiles};
-  dim3 pgrid(ntiles * (kTileRows / kPrepRows), batch);
-  dense_prep_kernel<<<pgrid, kPrepThreads, 0, stream>>>(pp);
+                     mask_batch_stride, mask_row_stride, eps, half, static_cast<uint8_t*>(workspace), ntiles, (int)units};
+  const int64_t groups = (units + kUnitsPerGroup - 1) / kUnitsPerGroup;
+  const int pblocks = (int)((groups + kPrepThreads / 8 - 1) / (kPrepThreads / 8));
+  dense_prep_kernel<<<pblocks, kPrepThreads, 0, stream>>>(pp);
   if (cudaGetLastError() != cudaSuccess) return HB_ERR_LAUNCH;
 
   AttnParams ap{};
