@@ -345,6 +345,65 @@ def time_w8a8(device, steps: int, warmup: int) -> dict:
             "l2": "flushed (256 MB write) before each pair"}
 
 
+# ----------------------------------------------------------------------------------------------- DiT clip
+def time_dit_clip(device, ff_quant: str, clips: int = 3) -> dict:
+    """Config 4: a whole 120 s clip (B=2 CFG pair, 2,584 latents + 64 memory tokens, 24 blocks, 8 pingpong
+    steps, random weights) through `hummingbird_b200.dit`; one denoise step is captured in a CUDA graph and
+    replayed per step. Returns ms per clip."""
+    import torch
+    from hummingbird_b200.config import DiTConfig
+    from hummingbird_b200.dit import DiT, ClipShape
+    cfg = DiTConfig(ff_quant=ff_quant)
+    shape = ClipShape()
+    model = DiT(cfg, shape, device)
+    g = torch.Generator(device=device).manual_seed(44)
+    static = model.prepare_static(torch.randn(shape.batch, shape.context, shape.context_dim, generator=g, device=device),
+                                  torch.randn(shape.batch, shape.context_dim, generator=g, device=device))
+    sched = DiT.schedule(shape.steps, device=device)
+    x_in = torch.randn(shape.batch, shape.io_channels, shape.latents, generator=g, device=device).to(torch.bfloat16)
+    eps = torch.randn(shape.steps, shape.batch, shape.io_channels, shape.latents, generator=g,
+                      device=device).to(torch.bfloat16)
+    t_cur = torch.zeros(shape.batch, device=device, dtype=torch.bfloat16)
+    t_nxt = torch.zeros_like(t_cur)
+    e_in = torch.empty_like(x_in)
+    side = torch.cuda.Stream(device)
+    side.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(side):
+        for _ in range(2):
+            x_out = model.step(x_in, t_cur, t_nxt, e_in, static)
+    torch.cuda.current_stream(device).wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        x_out = model.step(x_in, t_cur, t_nxt, e_in, static)
+    x0 = x_in.clone()
+
+    def clip():
+        x_in.copy_(x0)
+        for s in range(shape.steps):
+            t_cur.fill_(float(sched[s]))
+            t_nxt.fill_(float(sched[s + 1]))
+            e_in.copy_(eps[s])
+            graph.replay()
+            x_in.copy_(x_out)
+
+    clip()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(clips):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        clip()
+        b.record()
+        torch.cuda.synchronize()
+        times.append(a.elapsed_time(b))
+    finite = bool(torch.isfinite(x_in.float()).all())
+    del graph
+    return {"ms_per_clip": statistics.median(times), "config": "120 s clip: B=2 (CFG), 2,584 latents + 64 memory, "
+            "24 blocks, d 1024, 16 heads, 8 pingpong steps, 128 context tokens, random weights",
+            "mlp": "W8A8" if ff_quant == "w8a8" else "bf16 cuBLAS", "finite": finite,
+            "how": "one denoise step captured in a CUDA graph, replayed 8 times per clip"}
+
+
 # ----------------------------------------------------------------------------------------------- CPU baseline
 def cpu_band_baseline(qkv_dev, w, q_rows: int) -> dict:
     """The oracle port on the host cores over queries [0, q_rows) of the rank-0 workload."""
@@ -470,6 +529,8 @@ def main():
                 "dense_config1": time_dense(device, 50, 5, 1, 646, 16, 1024),
                 "dense_120s_block_call": time_dense(device, 20, 3, 2, 2648, 16, 1024),
                 "w8a8_config3": time_w8a8(device, 50, 5),
+                "dit_120s_clip_bf16_mlp": time_dit_clip(device, "none"),
+                "dit_120s_clip_w8a8_mlp": time_dit_clip(device, "w8a8"),
             }
         line["cpu_baseline"] = cpu_band_baseline(step.w.qkv, step.w, args.cpu_rows)
         from oracle.cpu_baseline import shutdown

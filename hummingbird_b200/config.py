@@ -21,7 +21,9 @@ class DiTConfig:
     num_memory_tokens: int = 64
     differential: bool = True
     qk_norm_eps: float = 1e-6
+    norm_eps: float = 1e-5
     rope_theta: float = 10000.0
+    fourier_dim: int = 256
     ff_mult: float = 4.0
     attention: Literal["xla", "fused", "cuda"] = "cuda"
     fused_min_tokens: int = 0  # the reference gates its TPU kernel at 800 tokens; the B200 kernel has no floor
