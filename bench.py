@@ -346,23 +346,21 @@ def time_w8a8(device, steps: int, warmup: int) -> dict:
 
 
 # ----------------------------------------------------------------------------------------------- DiT clip
-def time_dit_clip(device, ff_quant: str, clips: int = 3) -> dict:
-    """Config 4: a whole 120 s clip (B=2 CFG pair, 2,584 latents + 64 memory tokens, 24 blocks, 8 pingpong
-    steps, random weights) through `hummingbird_b200.dit`; one denoise step is captured in a CUDA graph and
-    replayed per step. Returns ms per clip."""
+def _dit_clip_runner(model, shape, device, seed: int = 44):
+    """Inputs of one clip and a `clip()` that denoises it: one denoise step captured in a CUDA graph (NCCL
+    all-to-alls included when the clip is split over ranks), replayed `shape.steps` times."""
     import torch
-    from hummingbird_b200.config import DiTConfig
-    from hummingbird_b200.dit import DiT, ClipShape
-    cfg = DiTConfig(ff_quant=ff_quant)
-    shape = ClipShape()
-    model = DiT(cfg, shape, device)
-    g = torch.Generator(device=device).manual_seed(44)
+    from hummingbird_b200.dit import DiT
+    g = torch.Generator(device=device).manual_seed(seed)
     static = model.prepare_static(torch.randn(shape.batch, shape.context, shape.context_dim, generator=g, device=device),
                                   torch.randn(shape.batch, shape.context_dim, generator=g, device=device))
-    sched = DiT.schedule(shape.steps, device=device)
-    x_in = torch.randn(shape.batch, shape.io_channels, shape.latents, generator=g, device=device).to(torch.bfloat16)
+    sched = [float(v) for v in DiT.schedule(shape.steps, device=device)]
+    a, b = model.latent_range()
+    x_full = torch.randn(shape.batch, shape.io_channels, shape.latents, generator=g, device=device).to(torch.bfloat16)
     eps = torch.randn(shape.steps, shape.batch, shape.io_channels, shape.latents, generator=g,
-                      device=device).to(torch.bfloat16)
+                      device=device).to(torch.bfloat16)[..., a:b].contiguous()
+    x0 = x_full[..., a:b].contiguous()
+    x_in = x0.clone()
     t_cur = torch.zeros(shape.batch, device=device, dtype=torch.bfloat16)
     t_nxt = torch.zeros_like(t_cur)
     e_in = torch.empty_like(x_in)
@@ -370,38 +368,181 @@ def time_dit_clip(device, ff_quant: str, clips: int = 3) -> dict:
     side.wait_stream(torch.cuda.current_stream(device))
     with torch.cuda.stream(side):
         for _ in range(2):
-            x_out = model.step(x_in, t_cur, t_nxt, e_in, static)
+            model.step(x_in, t_cur, t_nxt, e_in, static)
     torch.cuda.current_stream(device).wait_stream(side)
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph):
         x_out = model.step(x_in, t_cur, t_nxt, e_in, static)
-    x0 = x_in.clone()
 
     def clip():
         x_in.copy_(x0)
         for s in range(shape.steps):
-            t_cur.fill_(float(sched[s]))
-            t_nxt.fill_(float(sched[s + 1]))
+            t_cur.fill_(sched[s])
+            t_nxt.fill_(sched[s + 1])
             e_in.copy_(eps[s])
             graph.replay()
             x_in.copy_(x_out)
+        return x_in
 
+    return clip, graph
+
+
+def time_dit_clip(device, ff_quant: str, world: int = 1, clips: int = 3) -> dict:
+    """Config 4: a whole 120 s clip (B=2 CFG pair, 2,584 latents + 64 memory tokens, 24 blocks, 8 pingpong
+    steps, random weights) through `hummingbird_b200.dit`, split over `world` GPUs (token rows + head pairs,
+    two NCCL all-to-alls per block) when world > 1. Returns ms per clip (max over ranks)."""
+    import torch
+    import torch.distributed as dist
+    from hummingbird_b200.config import DiTConfig
+    from hummingbird_b200.dit import DiT, ClipShape
+    shape = ClipShape()
+    model = DiT(DiTConfig(ff_quant=ff_quant), shape, device, group=dist.group.WORLD if world > 1 else None)
+    clip, graph = _dit_clip_runner(model, shape, device)
     clip()
+    barrier(world)
     torch.cuda.synchronize()
     times = []
     for _ in range(clips):
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier(world)
         a.record()
-        clip()
+        x = clip()
         b.record()
         torch.cuda.synchronize()
-        times.append(a.elapsed_time(b))
-    finite = bool(torch.isfinite(x_in.float()).all())
+        times.append(max_over_ranks(a.elapsed_time(b), world))
+    finite = bool(torch.isfinite(x.float()).all())
     del graph
-    return {"ms_per_clip": statistics.median(times), "config": "120 s clip: B=2 (CFG), 2,584 latents + 64 memory, "
-            "24 blocks, d 1024, 16 heads, 8 pingpong steps, 128 context tokens, random weights",
+    torch.cuda.synchronize()
+    return {"ms_per_clip": statistics.median(times), "n_gpus": world,
+            "config": "120 s clip: B=2 (CFG), 2,584 latents + 64 memory, 24 blocks, d 1024, 16 heads, 8 pingpong "
+                      "steps, 128 context tokens, random weights",
             "mlp": "W8A8" if ff_quant == "w8a8" else "bf16 cuBLAS", "finite": finite,
-            "how": "one denoise step captured in a CUDA graph, replayed 8 times per clip"}
+            "glue": "fused row kernels (residual + RMSNorm + adaLN, GLU + quantise, head RMSNorm)",
+            "parallelism": f"one clip over {world} GPUs: token rows x{world}, self-attention head pairs x{world}, "
+                           "2 NCCL all-to-alls per block" if world > 1 else "single GPU",
+            "how": "one denoise step captured in a CUDA graph, replayed 8 times per clip; CUDA events, max over ranks"}
+
+
+SONG_LATENTS = 8184           # 380 s of audio
+SONG_BAND_ROWS = 261_888      # SAME-L decoder rows of a 380 s clip
+SONG_CLIPS = 8
+SONG_DECODER_LAYERS = 12
+
+
+def _song_band_layers(device, n_layers: int):
+    """`n_layers` SAME-L attention layers (d_model 512, 8 heads, window +-128) with random weights."""
+    import torch
+    from hummingbird_b200.workloads import inv_freq
+    g = torch.Generator(device=device).manual_seed(9)
+    layers = []
+    for _ in range(n_layers):
+        def norm():
+            return {"alpha": torch.tensor(0.5), "gamma": 1 + 0.02 * torch.randn(64, generator=g, device=device),
+                    "beta": 0.02 * torch.randn(64, generator=g, device=device)}
+        layers.append({"self_attn": {"to_qkv": {"weight": (torch.randn(5 * 512, 512, generator=g, device=device)
+                                                           / 512 ** 0.5).to(torch.bfloat16)},
+                                     "to_out": {"weight": (torch.randn(512, 512, generator=g, device=device)
+                                                           / 512 ** 0.5).to(torch.bfloat16)},
+                                     "q_norm": norm(), "k_norm": norm()},
+                       "rope_inv_freq": torch.from_numpy(inv_freq(16)).to(device)})
+    return layers
+
+
+def time_song(device, world: int, rank: int) -> dict:
+    """Config 5: a batch of 8 independent 380 s clips, clip-parallel over `world` GPUs (rank r renders clips
+    `shard_clips(8, world, r)`, no collective). Per clip: the DiT denoise at 8,184 latents (+64 memory
+    tokens, 24 blocks, 8 steps, W8A8 MLP, CUDA graph) and the 12 SAME-L attention layers of the decoder at
+    261,888 rows (to_qkv -> fused band kernel -> to_out). Returns ms for the batch (max over ranks)."""
+    import torch
+    from hummingbird_b200 import blocks, parallel as par
+    from hummingbird_b200.config import DiTConfig, SameConfig
+    from hummingbird_b200.dit import DiT, ClipShape
+    shape = ClipShape(latents=SONG_LATENTS)
+    model = DiT(DiTConfig(ff_quant="w8a8"), shape, device)
+    clip, graph = _dit_clip_runner(model, shape, device, seed=45)
+    layers = _song_band_layers(device, SONG_DECODER_LAYERS)
+    scfg = SameConfig(channels=512, c_mults=(1,), stride=127)  # d 512, 8 heads, window (sub_chunk_size) 128
+    x = torch.randn(1, SONG_BAND_ROWS, 512, generator=torch.Generator(device=device).manual_seed(46),
+                    device=device).to(torch.bfloat16)
+
+    def decoder():
+        y = x
+        for layer in layers:
+            y = blocks.same_l_attention(y, layer, scfg)
+        return y
+
+    mine = par.shard_clips(SONG_CLIPS, world, rank)
+    clip()
+    decoder()  # warm-up
+    barrier(world)
+    torch.cuda.synchronize()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    dit_ms = dec_ms = 0.0
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in mine:
+        ev[0].record()
+        lat = clip()
+        ev[1].record()
+        y = decoder()
+        ev[2].record()
+        torch.cuda.synchronize()
+        dit_ms += ev[0].elapsed_time(ev[1])
+        dec_ms += ev[1].elapsed_time(ev[2])
+    b.record()
+    torch.cuda.synchronize()
+    total = max_over_ranks(a.elapsed_time(b), world)
+    finite = {"dit": bool(torch.isfinite(lat.float()).all()), "decoder": bool(torch.isfinite(y.float()).all())}
+    del graph
+    torch.cuda.synchronize()
+    n = max(1, len(mine))
+    return {"ms_per_batch_of_8": total, "clips_per_s": SONG_CLIPS / (total * 1e-3), "n_gpus": world,
+            "dit_ms_per_clip": dit_ms / n, "decoder_attention_ms_per_clip": dec_ms / n, "finite": finite,
+            "config": "380 s song: 8 clips; per clip DiT B=2 (CFG), 8,184 latents + 64 memory, 24 blocks, d 1024, "
+                      "16 heads, 8 pingpong steps, W8A8 MLP; 12 SAME-L attention layers at 261,888 rows, d 512, "
+                      "8 heads, window +-128 (pre-normed input, to_qkv + band kernel + to_out); random weights",
+            "parallelism": f"clips data-parallel over {world} GPUs" if world > 1 else "single GPU, clips in sequence"}
+
+
+def time_band_song_layer(device, world: int, rank: int, steps: int = 20, warmup: int = 3) -> dict:
+    """Config 5's band attention, one layer at L = 261,888 (window +-128, 8 heads) sequence-sharded over
+    `world` GPUs (strong scaling): each rank's rows plus a 128-row halo per side by NCCL send/recv, then the
+    fused kernel. Returns ms per layer (halo exchange included; max over ranks) and TFLOP/s of all ranks."""
+    import torch
+    from hummingbird_b200 import band_attention as hb
+    from hummingbird_b200 import parallel as par
+    from hummingbird_b200.workloads import band_inputs
+    lay = par.band_layout(SONG_BAND_ROWS, world, rank, WINDOW)
+    w = band_inputs(device, seed=1, length=lay["q_count"], d_model=512, heads=HEADS, window=WINDOW,
+                    x_seed=(2, rank))
+    buf = torch.zeros(1, lay["rows"], 5 * HEADS * 64, dtype=torch.bfloat16, device=device)
+    buf[:, lay["before"]:lay["before"] + lay["q_count"]] = w.qkv
+    out = torch.empty(1, lay["q_count"], HEADS * 64, dtype=torch.bfloat16, device=device)
+    qn, kn = hb.pack_norm(w.q_norm, device), hb.pack_norm(w.k_norm, device)
+    freqs, lam = torch.from_numpy(w.inv_freq).to(device), torch.from_numpy(w.lam).to(device)
+
+    def one():
+        if world > 1:
+            par.halo_exchange(buf, lay, rank)
+        hb.band_attention_shard(buf, qn, kn, freqs, HEADS, 64, WINDOW, q_begin=lay["q_begin"], q_count=lay["q_count"],
+                                pos0=lay["pos0"], lam=lam, out=out)
+
+    for _ in range(warmup):
+        one()
+    barrier(world)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        one()
+    b.record()
+    torch.cuda.synchronize()
+    ms = max_over_ranks(a.elapsed_time(b) / steps, world)
+    flops = band_flops(SONG_BAND_ROWS, 0, SONG_BAND_ROWS)
+    return {"ms_per_layer": ms, "tflops": flops / (ms * 1e-3) / 1e12, "n_gpus": world,
+            "rows_per_gpu": lay["q_count"], "scaling": "strong",
+            "config": "SAME-L band differential attention at L=261,888 (380 s), d_model 512 (8 heads), window +-128",
+            "parallelism": f"sequence-sharded x{world}, NCCL halo send/recv" if world > 1 else "single GPU"}
 
 
 # ----------------------------------------------------------------------------------------------- CPU baseline
@@ -523,15 +664,18 @@ def main():
                      "tensor_frac_of_bf16": value / world / peaks["bf16_tflops"],
                      "tensor_peak_tflops": peaks["bf16_tflops"]},
     }
+    if not args.no_secondary:
+        paths = {}
+        if world == 1:
+            paths["dense_config1"] = time_dense(device, 50, 5, 1, 646, 16, 1024)
+            paths["dense_120s_block_call"] = time_dense(device, 20, 3, 2, 2648, 16, 1024)
+            paths["w8a8_config3"] = time_w8a8(device, 50, 5)
+            paths["dit_120s_clip_bf16_mlp"] = time_dit_clip(device, "none")
+        paths["dit_120s_clip_w8a8_mlp"] = time_dit_clip(device, "w8a8", world)
+        paths["band_380s_layer"] = time_band_song_layer(device, world, rank)
+        paths["song_380s_8_clips"] = time_song(device, world, rank)
+        line["paths"] = paths
     if world == 1 and rank == 0:
-        if not args.no_secondary:
-            line["paths"] = {
-                "dense_config1": time_dense(device, 50, 5, 1, 646, 16, 1024),
-                "dense_120s_block_call": time_dense(device, 20, 3, 2, 2648, 16, 1024),
-                "w8a8_config3": time_w8a8(device, 50, 5),
-                "dit_120s_clip_bf16_mlp": time_dit_clip(device, "none"),
-                "dit_120s_clip_w8a8_mlp": time_dit_clip(device, "w8a8"),
-            }
         line["cpu_baseline"] = cpu_band_baseline(step.w.qkv, step.w, args.cpu_rows)
         from oracle.cpu_baseline import shutdown
         shutdown()

@@ -17,7 +17,7 @@ PKG = Path(__file__).resolve().parent
 ROOT = PKG.parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libhb_b200.so"
-SOURCES = ["abi.cu", "attn_kernel.cu", "dense_attn.cu", "band_attn.cu", "band_fused.cu", "w8a8.cu"]
+SOURCES = ["abi.cu", "attn_kernel.cu", "dense_attn.cu", "band_attn.cu", "band_fused.cu", "w8a8.cu", "dit_glue.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -7,6 +7,10 @@ this library's fused differential kernel (`blocks.dit_self_attention`'s path); t
 differential cross-attention over the 128 hoisted context tokens (dit.py:203-215, 274-284) run as torch ops
 (cuBLAS / cuDNN-flash library kernels). No checkpoint is loaded: weights are N(0, 1 / fan_in) bf16 draws.
 
+With a process group of N ranks (one per GPU) one clip runs on all N: token-wise work is split by token rows
+and the self-attention by head pairs, with two all-to-alls per block (`hummingbird_b200.parallel`); each rank
+holds the latents of its token rows (`latent_range`) and `gather_latents` rebuilds the whole clip.
+
 Cast points follow the reference under the BF16 preset: bf16 activations, RMSNorm in fp32 cast back
 (dit.py:45-57), the adaLN gate `sigmoid(1 - gate)` (dit.py:227), cross K/V hoisted once per clip and k-normed
 (dit.py:274-284), the constant `to_local_embed` add on the non-memory tokens (dit.py:242-244).
@@ -17,11 +21,14 @@ import math
 from dataclasses import dataclass
 
 import torch
+import torch.distributed as dist
 import torch.nn.functional as F
 
 from hummingbird_b200 import dense_attention as hb_dense
+from hummingbird_b200 import dit_glue as glue
+from hummingbird_b200 import parallel as par
 from hummingbird_b200.config import DiTConfig
-from hummingbird_b200.w8a8 import W8A8Linear
+from hummingbird_b200.w8a8 import W8A8Linear, w8a8_gemm
 
 
 @dataclass(frozen=True)
@@ -55,10 +62,29 @@ def _expo_fourier(t: torch.Tensor, dim: int) -> torch.Tensor:
 
 
 class DiT:
-    """`dit_forward` with random weights; `static` state is built once per clip (`prepare_static`)."""
+    """`dit_forward` with random weights; `static` state is built once per clip (`prepare_static`).
 
-    def __init__(self, cfg: DiTConfig, shape: ClipShape, device, seed: int = 4):
+    `group`: a process group over which one clip is split (token rows + head pairs); None = this GPU alone.
+    `attend`: the differential self-attention (default: this library's kernel, `dense_attention`).
+    `glue`: "cuda" runs each block's residual / RMSNorm / adaLN / GLU steps as this library's fused row
+    kernels (`hummingbird_b200.dit_glue`); "torch" runs them as separate torch ops (the reference's op order)."""
+
+    def __init__(self, cfg: DiTConfig, shape: ClipShape, device, seed: int = 4, *, group=None, attend=None,
+                 glue: str = "cuda"):
         self.cfg, self.shape, self.device = cfg, shape, device
+        self.attend = attend or hb_dense.dense_attention
+        if glue not in ("cuda", "torch"):
+            raise ValueError(f"glue must be 'cuda' or 'torch', not {glue!r}")
+        self.glue = glue
+        self.group = group
+        self.world = dist.get_world_size(group) if group is not None else 1
+        self.rank = dist.get_rank(group) if group is not None else 0
+        self.seq = cfg.num_memory_tokens + shape.latents
+        self.t0, self.t1 = par.shard_tokens(self.seq, self.world, self.rank)
+        self.mem_rows = max(0, min(self.t1, cfg.num_memory_tokens) - self.t0)
+        if (cfg.num_heads // 2) % self.world or self.t1 - self.t0 <= self.mem_rows:
+            raise ValueError(f"a clip of {self.seq} tokens and {cfg.num_heads // 2} head pairs does not split "
+                             f"over {self.world} ranks (equal pair counts, latent rows on every rank)")
         g = torch.Generator(device=device).manual_seed(seed)
         d, h = cfg.embed_dim, cfg.num_heads
         io, ctx = shape.io_channels, shape.context_dim
@@ -96,6 +122,9 @@ class DiT:
             for name in ("pre_norm", "cross_attend_norm", "ff_norm"):
                 b[name + "_bf"] = b[name].to(torch.bfloat16)  # checkpoint norm weights are bf16
             b["cross_attn"]["q_norm_bf"] = b["cross_attn"]["q_norm"].to(torch.bfloat16)
+            if self.world > 1:  # rows grouped by destination rank: one batched GEMM fills the all-to-all buffer
+                rows = par.dest_major_qkv_rows(h, self.world).to(device)
+                b["self_attn"]["to_qkv_dest"] = b["self_attn"]["to_qkv"][rows].view(self.world, -1, d).transpose(1, 2)
             if cfg.ff_quant == "w8a8":
                 b["glu_q"] = W8A8Linear(b["glu"]["w"], b["glu"]["b"])
                 b["proj_out_q"] = W8A8Linear(b["proj_out"]["w"], b["proj_out"]["b"])
@@ -123,47 +152,114 @@ class DiT:
         """`nn.Sequential(Linear, SiLU, Linear)` without biases (dit.py:39-42)."""
         return F.silu(x @ layers[0].T) @ layers[1].T
 
+    # ------------------------------------------------------------------ sharding
+    def latent_range(self) -> tuple[int, int]:
+        """Latent indices [a, b) whose rows this rank holds (all of them on one GPU)."""
+        mem = self.cfg.num_memory_tokens
+        return max(self.t0, mem) - mem, self.t1 - mem
+
+    def gather_latents(self, x_local: torch.Tensor) -> torch.Tensor:
+        """All ranks' `(B, io, T_r)` latent slices -> the whole clip `(B, io, T)`."""
+        if self.world == 1:
+            return x_local
+        mem = self.cfg.num_memory_tokens
+        spans = [par.shard_tokens(self.seq, self.world, r) for r in range(self.world)]
+        widths = [t1 - max(t0, mem) for t0, t1 in spans]
+        padded = x_local.new_zeros(*x_local.shape[:2], max(widths))
+        padded[..., :x_local.shape[-1]] = x_local
+        parts = [torch.empty_like(padded) for _ in range(self.world)]
+        dist.all_gather(parts, padded, group=self.group)
+        return torch.cat([part[..., :w] for part, w in zip(parts, widths)], -1)
+
     # ------------------------------------------------------------------ denoiser
     def forward(self, x: torch.Tensor, t: torch.Tensor, static: dict) -> torch.Tensor:
-        """`dit_forward`: `(B, io, T)` latents and `(B,)` timesteps -> velocity `(B, io, T)` (dit.py:340-361)."""
+        """`dit_forward`: `(B, io, T_r)` latents (this rank's `latent_range`; all T on one GPU) and `(B,)`
+        timesteps -> velocity of the same shape (dit.py:340-361)."""
         cfg, p = self.cfg, self.p
         h = x.to(torch.bfloat16)
         h = torch.einsum("bct,oc->bot", h, p["preprocess_conv"]) + h
         h = h.transpose(1, 2) @ p["project_in"].T
-        mem = p["memory_tokens"].expand(h.shape[0], -1, -1)
-        h = torch.cat([mem, h], 1)
+        if self.mem_rows:
+            mem = p["memory_tokens"][self.t0:self.t0 + self.mem_rows].expand(h.shape[0], -1, -1)
+            h = torch.cat([mem, h], 1)
         temb = self._seq(p["to_timestep_embed"], _expo_fourier(t.to(torch.bfloat16), cfg.fourier_dim))
         gcond = self._seq(p["global_cond_embedder"], static["gcond_proj"] + temb)
-        for i, b in enumerate(self.blocks):
-            h = self._block(h, b, static, gcond, i)
-        h = h[:, cfg.num_memory_tokens:] @ p["project_out"].T
+        if self.glue == "cuda":
+            h = self._blocks_fused(h.contiguous(), static, gcond)
+        else:
+            for i, b in enumerate(self.blocks):
+                h = self._block(h, b, static, gcond, i)
+        h = h[:, self.mem_rows:] @ p["project_out"].T
         v = h.transpose(1, 2)
         return torch.einsum("bct,oc->bot", v, p["postprocess_conv"]) + v
 
     def _block(self, h, b, static, gcond, index):
         """One block with the elementwise steps fused where torch offers it: RMSNorm (fp32 statistics,
         `rms_norm`), `x * (1 + scale) + shift` and `h + y * sigmoid(1 - gate)` as single `addcmul`s."""
-        cfg, d, mem = self.cfg, self.cfg.embed_dim, self.cfg.num_memory_tokens
+        cfg, d = self.cfg, self.cfg.embed_dim
         ss, sh, gs, sf, shf, gf = (b["to_scale_shift_gate"] + gcond)[:, None, :].chunk(6, -1)
         x = torch.addcmul(sh, F.rms_norm(h, (d,), b["pre_norm_bf"], cfg.norm_eps), 1 + ss)
-        sa = b["self_attn"]
-        qkv = x @ sa["to_qkv"].T
-        att = hb_dense.dense_attention(qkv, sa["q_norm"], sa["k_norm"], static["lane_cos"], static["lane_sin"],
-                                       static["lane_mask"], cfg.num_heads, cfg.head_dim, cfg.rope_dim // 2,
-                                       cfg.qk_norm_eps)
-        h = torch.addcmul(h, att @ sa["to_out"].T, torch.sigmoid(1 - gs))
+        h = torch.addcmul(h, self._self_attn(x, b["self_attn"], static) @ b["self_attn"]["to_out"].T,
+                          torch.sigmoid(1 - gs))
         x = F.rms_norm(h, (d,), b["cross_attend_norm_bf"], cfg.norm_eps)
         h = h + self._cross(x, b["cross_attn"], static["cross_kv"][index])
-        h[:, mem:] += b["local"]
+        h[:, self.mem_rows:] += b["local"]
         x = torch.addcmul(shf, F.rms_norm(h, (d,), b["ff_norm_bf"], cfg.norm_eps), 1 + sf)
         return torch.addcmul(h, self._ff(x, b), torch.sigmoid(1 - gf))
+
+    def _blocks_fused(self, h, static, gcond):
+        """All blocks with the glue in fused kernels: each residual add is fused with the norm (and adaLN
+        modulation) that follows it, so `h` is updated in place and read once per residual."""
+        cfg, d = self.cfg, self.cfg.embed_dim
+        eps = cfg.norm_eps
+        conds = [(b["to_scale_shift_gate"] + gcond).contiguous() for b in self.blocks]  # (B, 6d) each
+
+        def part(c, i):  # scale_self, shift_self, gate_self, scale_ff, shift_ff, gate_ff (dit.py:230-232)
+            return c[:, i * d:(i + 1) * d]
+
+        c0 = conds[0]
+        x = glue.residual_norm(h, weight=self.blocks[0]["pre_norm_bf"], scale=part(c0, 0), shift=part(c0, 1), eps=eps)
+        for i, b in enumerate(self.blocks):
+            c = conds[i]
+            y = self._self_attn(x, b["self_attn"], static) @ b["self_attn"]["to_out"].T
+            x = glue.residual_norm(h, y=y, gate=part(c, 2), weight=b["cross_attend_norm_bf"], eps=eps)
+            y = self._cross(x, b["cross_attn"], static["cross_kv"][i])
+            x = glue.residual_norm(h, y=y, local=b["local"], local_row0=self.mem_rows, weight=b["ff_norm_bf"],
+                                   scale=part(c, 3), shift=part(c, 4), eps=eps)
+            y = self._ff(x, b)
+            if i + 1 < len(self.blocks):
+                nb, nc = self.blocks[i + 1], conds[i + 1]
+                x = glue.residual_norm(h, y=y, gate=part(c, 5), weight=nb["pre_norm_bf"], scale=part(nc, 0),
+                                       shift=part(nc, 1), eps=eps)
+            else:
+                glue.residual_norm(h, y=y, gate=part(c, 5), eps=eps)
+        return h
+
+    def _self_attn(self, x, sa, static):
+        """`to_qkv` -> fused differential attention (dit.py:185-200), before `to_out`. Over N ranks: this
+        rank's rows of every rank's `to_qkv` columns in one batched GEMM, all-to-all to head pairs, the kernel
+        on this rank's pairs over all rows, all-to-all back to this rank's rows."""
+        cfg = self.cfg
+        args = (sa["q_norm"], sa["k_norm"], static["lane_cos"], static["lane_sin"], static["lane_mask"])
+        if self.world == 1:
+            return self.attend(x @ sa["to_qkv"].T, *args, cfg.num_heads, cfg.head_dim, cfg.rope_dim // 2,
+                               cfg.qk_norm_eps)
+        bsz, rows, d = x.shape
+        send = torch.matmul(x.reshape(1, bsz * rows, d), sa["to_qkv_dest"])  # (N, B * rows, C)
+        qkv = par.tokens_to_pairs(send.view(self.world, bsz, rows, -1), self.seq, self.world, self.group)
+        att = self.attend(qkv, *args, cfg.num_heads // self.world, cfg.head_dim, cfg.rope_dim // 2, cfg.qk_norm_eps)
+        return par.pairs_to_tokens(att, self.seq, self.world, self.rank, self.group)
 
     def _cross(self, x, ca, kv):
         """Differential cross-attention, no RoPE, no mask (dit.py:203-215): SDPA(q) - SDPA(q_diff)."""
         cfg = self.cfg
         bsz, length, _ = x.shape
-        q2 = (x @ ca["to_q"].T).view(bsz, length, 2, cfg.num_heads, cfg.head_dim)
-        q2 = F.rms_norm(q2, (cfg.head_dim,), ca["q_norm_bf"], cfg.qk_norm_eps)
+        q2 = x @ ca["to_q"].T
+        if self.glue == "cuda":
+            q2 = glue.head_rms_norm(q2, ca["q_norm_bf"], cfg.qk_norm_eps)
+        q2 = q2.view(bsz, length, 2, cfg.num_heads, cfg.head_dim)
+        if self.glue == "torch":
+            q2 = F.rms_norm(q2, (cfg.head_dim,), ca["q_norm_bf"], cfg.qk_norm_eps)
         q, qd = q2[:, :, 0].transpose(1, 2), q2[:, :, 1].transpose(1, 2)
         k, kd, v = kv
         out = F.scaled_dot_product_attention(q, k, v) - F.scaled_dot_product_attention(qd, kd, v)
@@ -172,9 +268,17 @@ class DiT:
     def _ff(self, x, b):
         """`dit._feed_forward`: GLU `value * silu(gate)` (dit.py:218-221), W8A8 or bf16."""
         if self.cfg.ff_quant == "w8a8":
-            value, gate = b["glu_q"](x).chunk(2, -1)
+            g = b["glu_q"](x)
+            if self.glue == "cuda":  # value * silu(gate) and the per-token quantisation in one pass
+                q, s = glue.glu(g, quantize=True)
+                po = b["proj_out_q"]
+                return w8a8_gemm(q, s, po.qw, po.sw, po.bias).view(*x.shape[:-1], -1)
+            value, gate = g.chunk(2, -1)
             return b["proj_out_q"](value * F.silu(gate))
-        value, gate = (x @ b["glu"]["w"].T + b["glu"]["b"]).chunk(2, -1)
+        g = x @ b["glu"]["w"].T + b["glu"]["b"]
+        if self.glue == "cuda":
+            return glue.glu(g) @ b["proj_out"]["w"].T + b["proj_out"]["b"]
+        value, gate = g.chunk(2, -1)
         return (value * F.silu(gate)) @ b["proj_out"]["w"].T + b["proj_out"]["b"]
 
     # ------------------------------------------------------------------ sampler

@@ -8,6 +8,10 @@
   e.g. the reference's 12 pairs on 8 GPUs), computes them from its column slice of `to_qkv`, and
   `gather_pairs` all-gathers the (B, L, pairs * 128) pieces into the full (B, L, H * 64) output.
 * clips — data parallel: rank r renders clips `shard_clips(n, N, r)`; no collective.
+* the DiT denoiser of one clip — token rows `shard_tokens(L, N, r)` for every token-wise op (projections,
+  adaLN, cross-attention, MLP) and head pairs `shard_pairs(P, N, r)` for the self-attention, switched by two
+  all-to-alls per block (`tokens_to_pairs`, `pairs_to_tokens`): rank r sends each rank s the `to_qkv`
+  columns of s's pairs for its own rows, and gets back its rows of every rank's attention output.
 
 The reference has no parallelism at all (it runs one TPU chip); these follow the partitions its kernels
 admit: head pairs are independent (dense_attention.py:126-127), band rows depend only on +-window rows
@@ -30,6 +34,43 @@ def shard_rows(length: int, world: int, rank: int, align: int = 128) -> tuple[in
 def shard_pairs(pairs: int, world: int, rank: int) -> tuple[int, int]:
     """Head-pair range [begin, end) of `rank` (contiguous, sizes differ by at most one)."""
     return pairs * rank // world, pairs * (rank + 1) // world
+
+
+def shard_tokens(length: int, world: int, rank: int) -> tuple[int, int]:
+    """Token range [t0, t1) of `rank` for the DiT's token-wise ops (sizes differ by at most one)."""
+    return length * rank // world, length * (rank + 1) // world
+
+
+def dest_major_qkv_rows(heads: int, world: int) -> torch.Tensor:
+    """Row order of `to_qkv` whose output columns are grouped by destination rank: rank s's block holds the
+    q, k, v, q_diff, k_diff columns of its pairs (each block in the kernel's section order)."""
+    pairs = heads // 2
+    return torch.cat([qkv_columns_for_pairs(heads, *shard_pairs(pairs, world, s)) for s in range(world)])
+
+
+def tokens_to_pairs(send: torch.Tensor, length: int, world: int, group=None) -> torch.Tensor:
+    """All-to-all from token shards to head-pair shards.
+
+    `send` is `(world, B, rows_r, C)`: block s holds this rank's rows of the `C` `to_qkv` columns of rank s's
+    pairs (equal pair counts on every rank). Returns `(B, length, C)`: every row of this rank's pairs."""
+    n, b, rows, c = send.shape
+    lens = [t1 - t0 for t0, t1 in (shard_tokens(length, world, s) for s in range(world))]
+    recv = send.new_empty(b * length * c)
+    dist.all_to_all_single(recv, send.reshape(-1), [b * l * c for l in lens], [b * rows * c] * world, group=group)
+    return torch.cat([blk.view(b, l, c) for blk, l in zip(recv.split([b * l * c for l in lens]), lens)], 1)
+
+
+def pairs_to_tokens(att: torch.Tensor, length: int, world: int, rank: int, group=None) -> torch.Tensor:
+    """All-to-all back: `att` `(B, length, W)` is this rank's pairs for every row; returns `(B, rows_r, world * W)`,
+    this rank's rows of every rank's pairs in pair order (the full attention output of its rows)."""
+    b, _, w = att.shape
+    bounds = [shard_tokens(length, world, s) for s in range(world)]
+    r0, r1 = bounds[rank]
+    send = torch.cat([att[:, t0:t1].reshape(-1) for t0, t1 in bounds])
+    recv = att.new_empty(world * b * (r1 - r0) * w)
+    dist.all_to_all_single(recv, send, [b * (r1 - r0) * w] * world, [b * (t1 - t0) * w for t0, t1 in bounds],
+                           group=group)
+    return recv.view(world, b, r1 - r0, w).permute(1, 2, 0, 3).reshape(b, r1 - r0, world * w)
 
 
 def shard_clips(n_clips: int, world: int, rank: int) -> range:

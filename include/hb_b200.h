@@ -131,6 +131,36 @@ int hb_w8a8_gemm(const void* qx, int64_t ldqx, const float* sx, const void* qw, 
                  const void* bias, void* out, int64_t ldo, int32_t* acc_out, int64_t ldacc, int M, int N, int K,
                  cudaStream_t stream);
 
+/* ---- DiT block glue (the elementwise steps around the kernels above) ------------------------------------ */
+/* No reference counterpart as entry points: the reference runs these steps as separate XLA ops inside
+ * `dit._block` (dit.py:224-250); here each fuses several of them into one pass over the activation rows.
+ * All tensors bf16, row-major; rows = B * rows_per_batch; batch b = row / rows_per_batch.
+ *
+ * In place on h [rows, d] (ld ldh), then an optional normalised copy x [rows, d] (ld ldx):
+ *   h <- h + y * sigmoid(1 - gate[b])        if y (gate [B, d] with row stride ldc, NULL = no gate)
+ *   h <- h + local                           on rows with (row % rows_per_batch) >= local_row0, if local
+ *   x <- RMSNorm(h, eps) * weight            if x (weight [d])
+ *   x <- x * (1 + scale[b]) + shift[b]       if scale and shift ([B, d], row stride ldc)
+ * The adaLN pre-norms (dit.py:234-235, 247-248), the gated residuals (dit.py:237, 250), the cross-attention
+ * residual with `to_local_embed` (dit.py:240, 244) and the norm before it (dit.py:239).
+ * d a multiple of 256, <= 2048. */
+int hb_dit_residual_norm(void* h, int64_t ldh, const void* y, int64_t ldy, const void* gate, const void* scale,
+                         const void* shift, int64_t ldc, const void* local, int local_row0, const void* weight,
+                         void* x, int64_t ldx, int rows, int rows_per_batch, int d, float eps, cudaStream_t stream);
+
+/* GLU of `dit._feed_forward` (dit.py:218-221): per row of glu [rows, 2F] (value = columns [0, F), gate =
+ * [F, 2F)), z = value * silu(gate) rounded to bf16; written to z [rows, F] (ld ldz) OR quantised per row
+ * with hb_quant_rows_int8's rules into q int8 [rows, F] (ld ldq bytes) and scale fp32 [rows] (exactly one
+ * of z, q). F a multiple of 8, <= 8192. */
+int hb_glu_rows(const void* glu, int64_t ldg, int rows, int F, void* z, int64_t ldz, void* q, int64_t ldq,
+                float* scale, cudaStream_t stream);
+
+/* `dit._rms` over every 64-dim head of x [rows, heads * 64] (ld ldx) with weight [64] (bf16), to out
+ * (ld ldo; may equal x): the q / q_diff norm that `_attend` applies to the cross-attention queries
+ * (dit.py:150-176, 203-215). */
+int hb_head_rms_norm(const void* x, int64_t ldx, int rows, int heads, const void* weight, float eps, void* out,
+                     int64_t ldo, cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

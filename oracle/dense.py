@@ -85,8 +85,9 @@ def softmax_attend(q: np.ndarray, k: np.ndarray, v: np.ndarray, bf16_weights: bo
 
 def dense_branches(qkv: np.ndarray, q_weight: np.ndarray, k_weight: np.ndarray, freqs: np.ndarray,
                    valid: np.ndarray, num_heads: int, eps: float,
-                   fused_casts: bool = False) -> tuple[np.ndarray, np.ndarray]:
-    """The two softmax branches A (q, k) and B (q_diff, k_diff) with the shared masked v, `(B, H, L, 64)`.
+                   fused_casts: bool = False, queries=None) -> tuple[np.ndarray, np.ndarray]:
+    """The two softmax branches A (q, k) and B (q_diff, k_diff) with the shared masked v, `(B, H, L, 64)`
+    (or `(B, H, len(queries), 64)` for the query rows `queries` only; every key is still attended).
 
     `fused_casts=False` is the XLA path in fp32 (the parity target). `fused_casts=True` adds the cast points
     of the reference's fused kernel (dense_attention.py:61-83): RMSNorm output -> bf16, RoPE output -> bf16,
@@ -98,13 +99,16 @@ def dense_branches(qkv: np.ndarray, q_weight: np.ndarray, k_weight: np.ndarray, 
     q, k, qd, kd = (cast(apply_rope(cast(rms_norm(t, w, eps)), cos, sin))
                     for t, w in ((q, q_weight), (k, k_weight), (qd, q_weight), (kd, k_weight)))
     v = cast(v * np.asarray(valid, np.float64)[:, None, :, None])
+    if queries is not None:
+        q, qd = q[:, :, queries], qd[:, :, queries]
     return softmax_attend(q, k, v, fused_casts), softmax_attend(qd, kd, v, fused_casts)
 
 
 def dense_diff_attention(qkv: np.ndarray, q_weight: np.ndarray, k_weight: np.ndarray, freqs: np.ndarray,
                          valid: np.ndarray, num_heads: int, eps: float = 1e-6,
-                         lam: np.ndarray | None = None, fused_casts: bool = False) -> np.ndarray:
-    """`(B, L, 5 * H * 64)` -> `(B, L, H * 64)` fp32: `A - lambda[pair] * B` per head (pair = head // 2)."""
-    a, b = dense_branches(qkv, q_weight, k_weight, freqs, valid, num_heads, eps, fused_casts)
+                         lam: np.ndarray | None = None, fused_casts: bool = False, queries=None) -> np.ndarray:
+    """`(B, L, 5 * H * 64)` -> `(B, L, H * 64)` fp32: `A - lambda[pair] * B` per head (pair = head // 2);
+    with `queries`, only those rows: `(B, len(queries), H * 64)`."""
+    a, b = dense_branches(qkv, q_weight, k_weight, freqs, valid, num_heads, eps, fused_casts, queries)
     lam_h = np.ones(num_heads) if lam is None else np.repeat(np.asarray(lam, np.float64), 2)
     return merge_heads(a - lam_h[None, :, None, None] * b).astype(np.float32)

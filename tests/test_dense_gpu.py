@@ -86,6 +86,23 @@ def test_dense_long_sequence_against_oracle(cuda_lib):
     check_attn(to_np(out), ref)
 
 
+def test_dense_380s_length_against_oracle_on_sampled_rows(cuda_lib):
+    """B=2, L=8,248 (the 380 s DiT self-attention length: 65 key tiles, ragged tail), 4 heads, lambda; the
+    oracle on sampled query rows (first and last tiles, a middle block) against every key."""
+    from hummingbird_b200.workloads import dense_inputs
+    from hummingbird_b200 import dense_attention as hb
+    length = 8248
+    w = dense_inputs("cuda", seed=6, batch=2, length=length, d_model=256, heads=4, masked_tail=64)
+    cos, sin, mask = hb.tables(length, f32_cuda(w.inv_freq), f32_cuda(w.valid))
+    out = to_np(hb.dense_attention(w.qkv, f32_cuda(w.q_weight), f32_cuda(w.k_weight), cos, sin, mask, w.heads, 64,
+                                   w.half, w.eps, lam=f32_cuda(w.lam)))
+    assert np.isfinite(out).all()
+    rows = np.r_[0:64, 4100:4164, length - 72:length]
+    ref = odense.dense_diff_attention(to_np(w.qkv), w.q_weight, w.k_weight, w.inv_freq, w.valid, w.heads, w.eps,
+                                      lam=w.lam, queries=rows)
+    check_attn(out[:, rows], ref)
+
+
 def test_dense_rejects_bad_shapes(cuda_lib):
     from hummingbird_b200 import dense_attention as hb
     qkv = torch.zeros(1, 8, 5 * 4 * 64, dtype=torch.bfloat16, device="cuda")
