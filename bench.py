@@ -348,7 +348,9 @@ def time_w8a8(device, steps: int, warmup: int) -> dict:
 # ----------------------------------------------------------------------------------------------- DiT clip
 def _dit_clip_runner(model, shape, device, seed: int = 44):
     """Inputs of one clip and a `clip()` that denoises it: one denoise step captured in a CUDA graph (NCCL
-    all-to-alls included when the clip is split over ranks), replayed `shape.steps` times."""
+    all-to-alls included when the clip is split over ranks), replayed `shape.steps` times. Returns `clip` and
+    the objects the graph reads (the graph itself, the per-clip static tensors): the caller keeps them alive
+    while it replays and releases them together."""
     import torch
     from hummingbird_b200.dit import DiT
     g = torch.Generator(device=device).manual_seed(seed)
@@ -384,7 +386,7 @@ def _dit_clip_runner(model, shape, device, seed: int = 44):
             x_in.copy_(x_out)
         return x_in
 
-    return clip, graph
+    return clip, (graph, static)
 
 
 def time_dit_clip(device, ff_quant: str, world: int = 1, clips: int = 3) -> dict:
@@ -397,7 +399,7 @@ def time_dit_clip(device, ff_quant: str, world: int = 1, clips: int = 3) -> dict
     from hummingbird_b200.dit import DiT, ClipShape
     shape = ClipShape()
     model = DiT(DiTConfig(ff_quant=ff_quant), shape, device, group=dist.group.WORLD if world > 1 else None)
-    clip, graph = _dit_clip_runner(model, shape, device)
+    clip, held = _dit_clip_runner(model, shape, device)
     clip()
     barrier(world)
     torch.cuda.synchronize()
@@ -411,7 +413,7 @@ def time_dit_clip(device, ff_quant: str, world: int = 1, clips: int = 3) -> dict
         torch.cuda.synchronize()
         times.append(max_over_ranks(a.elapsed_time(b), world))
     finite = bool(torch.isfinite(x.float()).all())
-    del graph
+    del clip, held
     torch.cuda.synchronize()
     return {"ms_per_clip": statistics.median(times), "n_gpus": world,
             "config": "120 s clip: B=2 (CFG), 2,584 latents + 64 memory, 24 blocks, d 1024, 16 heads, 8 pingpong "
@@ -459,7 +461,7 @@ def time_song(device, world: int, rank: int) -> dict:
     from hummingbird_b200.dit import DiT, ClipShape
     shape = ClipShape(latents=SONG_LATENTS)
     model = DiT(DiTConfig(ff_quant="w8a8"), shape, device)
-    clip, graph = _dit_clip_runner(model, shape, device, seed=45)
+    clip, held = _dit_clip_runner(model, shape, device, seed=45)
     layers = _song_band_layers(device, SONG_DECODER_LAYERS)
     scfg = SameConfig(channels=512, c_mults=(1,), stride=127)  # d 512, 8 heads, window (sub_chunk_size) 128
     x = torch.randn(1, SONG_BAND_ROWS, 512, generator=torch.Generator(device=device).manual_seed(46),
@@ -494,7 +496,7 @@ def time_song(device, world: int, rank: int) -> dict:
     torch.cuda.synchronize()
     total = max_over_ranks(a.elapsed_time(b), world)
     finite = {"dit": bool(torch.isfinite(lat.float()).all()), "decoder": bool(torch.isfinite(y.float()).all())}
-    del graph
+    del clip, held
     torch.cuda.synchronize()
     n = max(1, len(mine))
     return {"ms_per_batch_of_8": total, "clips_per_s": SONG_CLIPS / (total * 1e-3), "n_gpus": world,

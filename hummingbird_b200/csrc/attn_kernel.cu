@@ -211,35 +211,31 @@ __global__ void __launch_bounds__(kThreads, 1) diff_attention_kernel(const AttnP
       if (!ok) break;
       tc_fence_after();
       const int k0 = (kt0 + i) * kTileRows;
-      float s[128];
-      {
-        uint32_t r[32];
+      // raw fp32 scores of this row's 128 keys: four loads in flight, one wait
+      uint32_t r[4][32];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          tmem_ld32(tS + 32 * c, r);
-          tmem_wait_ld();
-#pragma unroll
-          for (int j = 0; j < 32; ++j) s[32 * c + j] = __uint_as_float(r[j]);
-        }
-      }
+      for (int c = 0; c < 4; ++c) tmem_ld32(tS + 32 * c, r[c]);
+      tmem_wait_ld();
       bool full = (k0 + kTileRows - 1) < p.rows;
       if (p.window >= 0) full = full && (k0 >= q_hi_w - p.window) && (k0 + kTileRows - 1 <= q_lo_w + p.window);
-      float rmax = -INFINITY;
-      if (full) {
-#pragma unroll
-        for (int j = 0; j < 128; ++j) {
-          s[j] *= kScoreScale;
-          rmax = fmaxf(rmax, s[j]);
-        }
-      } else {
+      if (!full) {
 #pragma unroll
         for (int j = 0; j < 128; ++j) {
           const int k = k0 + j;
           const bool in = k < p.rows && (p.window < 0 || abs(k - q) <= p.window);
-          s[j] = in ? s[j] * kScoreScale : -INFINITY;
-          rmax = fmaxf(rmax, s[j]);
+          if (!in) r[j >> 5][j & 31] = 0xff800000u;  // -inf
         }
       }
+      // row max of the raw scores: four independent chains of three-input maxima (scale > 0 commutes)
+      float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+      for (int j = 0; j < 128; j += 8) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          mx[u] = fmax3(mx[u], __uint_as_float(r[j >> 5][(j & 31) + 2 * u]),
+                        __uint_as_float(r[j >> 5][(j & 31) + 2 * u + 1]));
+      }
+      const float rmax = fmaxf(fmax3(mx[0], mx[1], mx[2]), mx[3]) * kScoreScale;
       const float m_new = fmaxf(m, rmax);
       const bool upd = m_new > m + kRescaleThreshold;
       float alpha = 1.f;
@@ -247,23 +243,28 @@ __global__ void __launch_bounds__(kThreads, 1) diff_attention_kernel(const AttnP
         alpha = (m == -INFINITY) ? 0.f : ex2_approx(m - m_new);
         m = m_new;
       }
-      const float msafe = (m == -INFINITY) ? 0.f : m;
-      float rs = 0.f;
-      {
+      const float nm = (m == -INFINITY) ? 0.f : -m;
+      // P = exp2(s * scale - m): packed FMA per key pair, bf16 pairs into the first 64 columns of S;
+      // the row sum in two packed accumulators (four partial sums)
+      float rs[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
         uint32_t pk[32];
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const float p0 = ex2_approx(s[64 * c + 2 * j] - msafe);
-            const float p1 = ex2_approx(s[64 * c + 2 * j + 1] - msafe);
-            rs += p0 + p1;
-            pk[j] = pack_bf16x2(p0, p1);
-          }
-          tmem_st32(tS + 32 * c, pk);
+        for (int j = 0; j < 32; ++j) {
+          const int e = 64 * c + 2 * j;
+          float x0, x1;
+          ffma2(x0, x1, __uint_as_float(r[e >> 5][e & 31]), __uint_as_float(r[e >> 5][(e & 31) + 1]), kScoreScale,
+                kScoreScale, nm, nm);
+          const float p0 = ex2_approx(x0), p1 = ex2_approx(x1);
+          const int a = (j & 1) * 2;
+          fadd2(rs[a], rs[a + 1], rs[a], rs[a + 1], p0, p1);
+          pk[j] = pack_bf16x2(p0, p1);
         }
+        tmem_st32(tS + 32 * c, pk);
       }
-      l = l * alpha + rs;
+      const float rsum = (rs[0] + rs[1]) + (rs[2] + rs[3]);
+      l = l * alpha + rsum;
       if (i > 0 && __any_sync(0xffffffffu, upd)) {
         uint32_t o[32];
 #pragma unroll

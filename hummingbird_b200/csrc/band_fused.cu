@@ -415,8 +415,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0 && quad == 0) TRACE(2 + br, 100 + kt, t0);
         tc_fence_after();
         const int k0 = kt * kTileRows;
-        // pass 1: row max over in-band keys; 32-key chunks outside the band for the whole warp are skipped
-        float rmax = -INFINITY;
+        // pass 1: row max over in-band keys; 32-key chunks outside the band for the whole warp are skipped,
+        // chunks inside it for every lane of the warp need no mask (two chains of three-input maxima)
+        float mx0 = -INFINITY, mx1 = -INFINITY;
         uint32_t r[32];
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
@@ -425,12 +426,19 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t bits = band_bits(kc, q, p.window, p.rows);
           tmem_ld32(tS + 32 * c, r);
           tmem_wait_ld();
+          if (!__all_sync(0xffffffffu, bits == 0xffffffffu)) {
 #pragma unroll
-          for (int e = 0; e < 32; ++e)
-            rmax = fmaxf(rmax, (bits >> e) & 1u ? __uint_as_float(r[e]) : -INFINITY);
+            for (int e = 0; e < 32; ++e)
+              if (!((bits >> e) & 1u)) r[e] = 0xff800000u;  // -inf
+          }
+#pragma unroll
+          for (int e = 0; e < 32; e += 4) {
+            mx0 = fmax3(mx0, __uint_as_float(r[e]), __uint_as_float(r[e + 1]));
+            mx1 = fmax3(mx1, __uint_as_float(r[e + 2]), __uint_as_float(r[e + 3]));
+          }
         }
         if (lane == 0 && quad == 0) TRACE(2 + br, 500 + kt, t0);
-        rmax *= kScoreScale;
+        const float rmax = fmaxf(mx0, mx1) * kScoreScale;
         const float m_new = fmaxf(m, rmax);
         const bool upd = m_new > m + kRescaleThreshold;
         float alpha = 1.f;
@@ -438,9 +446,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           alpha = (m == -INFINITY) ? 0.f : ex2_approx(m - m_new);
           m = m_new;
         }
-        const float msafe = (m == -INFINITY) ? 0.f : m;
-        // pass 2: P = exp2(s * scale - m) as bf16 into the first 64 columns of S (in place)
-        float rs = 0.f;
+        const float nm = (m == -INFINITY) ? 0.f : -m;
+        // pass 2: P = exp2(s * scale - m) as bf16 into the first 64 columns of S (in place); packed FMA per key
+        // pair and two packed row-sum accumulators
+        float rs0 = 0.f, rs1 = 0.f, rs2 = 0.f, rs3 = 0.f;
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
           const int kc = k0 + 32 * c;
@@ -452,18 +461,26 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t bits = band_bits(kc, q, p.window, p.rows);
             tmem_ld32(tS + 32 * c, r);
             tmem_wait_ld();
+            if (!__all_sync(0xffffffffu, bits == 0xffffffffu)) {
+#pragma unroll
+              for (int e = 0; e < 32; ++e)
+                if (!((bits >> e) & 1u)) r[e] = 0xff800000u;
+            }
 #pragma unroll
             for (int e = 0; e < 16; ++e) {
-              const float s0 = (bits >> (2 * e)) & 1u ? fmaf(__uint_as_float(r[2 * e]), kScoreScale, -msafe) : -INFINITY;
-              const float s1 =
-                  (bits >> (2 * e + 1)) & 1u ? fmaf(__uint_as_float(r[2 * e + 1]), kScoreScale, -msafe) : -INFINITY;
-              const float p0 = ex2_approx(s0), p1 = ex2_approx(s1);
-              rs += p0 + p1;
+              float x0, x1;
+              ffma2(x0, x1, __uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1]), kScoreScale, kScoreScale, nm, nm);
+              const float p0 = ex2_approx(x0), p1 = ex2_approx(x1);
+              if (e & 1)
+                fadd2(rs2, rs3, rs2, rs3, p0, p1);
+              else
+                fadd2(rs0, rs1, rs0, rs1, p0, p1);
               pk[e] = pack_bf16x2(p0, p1);
             }
           }
           tmem_st16(tS + 16 * c, pk);
         }
+        const float rs = (rs0 + rs1) + (rs2 + rs3);
         l = l * alpha + rs;
         if (lane == 0 && quad == 0) TRACE(2 + br, 600 + kt, t0);
         if (kt > x.klo && __any_sync(0xffffffffu, upd)) {
