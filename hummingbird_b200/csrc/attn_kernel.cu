@@ -256,7 +256,13 @@ __global__ void __launch_bounds__(kThreads, 1) diff_attention_kernel(const AttnP
           float x0, x1;
           ffma2(x0, x1, __uint_as_float(r[e >> 5][e & 31]), __uint_as_float(r[e >> 5][(e & 31) + 1]), kScoreScale,
                 kScoreScale, nm, nm);
-          const float p0 = ex2_approx(x0), p1 = ex2_approx(x1);
+          float p0, p1;
+          if ((j & kPolyMask) == kPolyMask) {  // a share of the exponentials on the FMA pipe
+            exp2_poly2(x0, x1, p0, p1);
+          } else {
+            p0 = ex2_approx(x0);
+            p1 = ex2_approx(x1);
+          }
           const int a = (j & 1) * 2;
           fadd2(rs[a], rs[a + 1], rs[a], rs[a + 1], p0, p1);
           pk[j] = pack_bf16x2(p0, p1);

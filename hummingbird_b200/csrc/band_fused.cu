@@ -470,7 +470,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int e = 0; e < 16; ++e) {
               float x0, x1;
               ffma2(x0, x1, __uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1]), kScoreScale, kScoreScale, nm, nm);
-              const float p0 = ex2_approx(x0), p1 = ex2_approx(x1);
+              float p0, p1;
+              if ((e & kPolyMask) == kPolyMask) {  // a share of the exponentials on the FMA pipe
+                exp2_poly2(x0, x1, p0, p1);
+              } else {
+                p0 = ex2_approx(x0);
+                p1 = ex2_approx(x1);
+              }
               if (e & 1)
                 fadd2(rs2, rs3, rs2, rs3, p0, p1);
               else

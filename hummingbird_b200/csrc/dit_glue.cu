@@ -164,27 +164,28 @@ __global__ void __launch_bounds__(kGluThreads) glu_rows_kernel(const uint16_t* _
     }
     if constexpr (!kQuant) *reinterpret_cast<uint4*>(z + (size_t)r * ldz + k) = pack8(zv[i]);
   }
-  if constexpr (!kQuant) return;
+  if constexpr (kQuant) {
 #pragma unroll
-  for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-  if (lane == 0) warp_max[tid >> 5] = amax;
-  __syncthreads();
-  amax = warp_max[0];
+    for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    if (lane == 0) warp_max[tid >> 5] = amax;
+    __syncthreads();
+    amax = warp_max[0];
 #pragma unroll
-  for (int w = 1; w < kGluThreads / 32; ++w) amax = fmaxf(amax, warp_max[w]);
-  const float s = amax == 0.f ? 1.f : __fdiv_rn(amax, 127.f);
-  if (tid == 0) scale[r] = s;
+    for (int w = 1; w < kGluThreads / 32; ++w) amax = fmaxf(amax, warp_max[w]);
+    const float s = amax == 0.f ? 1.f : __fdiv_rn(amax, 127.f);
+    if (tid == 0) scale[r] = s;
 #pragma unroll
-  for (int i = 0; i < kGluChunks; ++i) {
-    const int k = (tid + kGluThreads * i) * 8;
-    if (k >= F) continue;
-    uint32_t packed[2] = {0u, 0u};
+    for (int i = 0; i < kGluChunks; ++i) {
+      const int k = (tid + kGluThreads * i) * 8;
+      if (k >= F) continue;
+      uint32_t packed[2] = {0u, 0u};
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const float qv = fminf(fmaxf(rintf(__fdiv_rn(zv[i][e], s)), -127.f), 127.f);
-      packed[e >> 2] |= (static_cast<uint32_t>(static_cast<int>(qv)) & 0xFFu) << (8 * (e & 3));
+      for (int e = 0; e < 8; ++e) {
+        const float qv = fminf(fmaxf(rintf(__fdiv_rn(zv[i][e], s)), -127.f), 127.f);
+        packed[e >> 2] |= (static_cast<uint32_t>(static_cast<int>(qv)) & 0xFFu) << (8 * (e & 3));
+      }
+      *reinterpret_cast<uint2*>(q + (size_t)r * ldq + k) = make_uint2(packed[0], packed[1]);
     }
-    *reinterpret_cast<uint2*>(q + (size_t)r * ldq + k) = make_uint2(packed[0], packed[1]);
   }
 }
 

@@ -269,6 +269,33 @@ __device__ __forceinline__ void fmul2(float& d0, float& d1, float a0, float a1, 
       : "=f"(d0), "=f"(d1)
       : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
 }
+// 2^x for two values on the FMA / integer pipes instead of the MUFU unit (used for a share of the softmax
+// exponentials so the two pipes split the load). Range reduction x = j + f with j = rint(x) (adding and
+// subtracting 1.5 * 2^23 rounds to an integer held in the low mantissa bits) and |f| <= 1/2; 2^f by a
+// degree-3 polynomial fitted for this library to minimise the relative error on [-1/2, 1/2] (Lawson's
+// iteratively reweighted least squares; max relative error 7.5e-5, far below bf16's 2^-9 for P); 2^j
+// added to the exponent field. Inputs are clamped to >= -125, so masked keys (x = -inf) get a weight of
+// ~2^-125 instead of 0: below 2^-125 of the row maximum, invisible in fp32 sums and bf16 outputs.
+__device__ __forceinline__ void exp2_poly2(float x0, float x1, float& p0, float& p1) {
+  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
+  constexpr float c0 = 0.9999281f, c1 = 0.69326097f, c2 = 0.24261054f, c3 = 0.05517132f;
+  x0 = fmaxf(x0, -125.f);
+  x1 = fmaxf(x1, -125.f);
+  float t0, t1, j0, j1, f0, f1, q0, q1;
+  fadd2(t0, t1, x0, x1, kRound, kRound);
+  fadd2(j0, j1, t0, t1, -kRound, -kRound);
+  ffma2(f0, f1, j0, j1, -1.f, -1.f, x0, x1);
+  ffma2(q0, q1, c3, c3, f0, f1, c2, c2);
+  ffma2(q0, q1, q0, q1, f0, f1, c1, c1);
+  ffma2(q0, q1, q0, q1, f0, f1, c0, c0);
+  p0 = __uint_as_float(__float_as_uint(q0) + (__float_as_uint(t0) << 23));
+  p1 = __uint_as_float(__float_as_uint(q1) + (__float_as_uint(t1) << 23));
+}
+// Share of the softmax exponentials computed by exp2_poly2: key pairs j with (j & kPolyMask) == kPolyMask.
+#ifndef HB_POLY_MASK
+#define HB_POLY_MASK 3
+#endif
+constexpr int kPolyMask = HB_POLY_MASK;
 // Three-input maximum (sm_100).
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float d;
