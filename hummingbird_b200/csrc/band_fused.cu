@@ -32,20 +32,23 @@
 namespace hb {
 
 #ifdef HB_TRACE
-// Debug builds only (-DHB_TRACE): clock64 timestamps of pipeline events of CTA 0, one row per traced thread.
+// Debug builds only (-DHB_TRACE): %clock timestamps of pipeline events, one slot per traced thread, kept in
+// shared memory while the kernel runs (no global traffic) and copied out by CTA 0 at the end.
 __device__ unsigned int g_trace[8][2048];
 __device__ unsigned int g_trace_n[8];
-#define TRACE(slot, id, t0)                                                                         \
-  do {                                                                                              \
-    if (blockIdx.x == 0) {                                                                          \
-      const unsigned n_ = g_trace_n[slot]++;                                                        \
-      if (n_ < 1024) {                                                                              \
-        g_trace[slot][2 * n_] = (id);                                                               \
-        g_trace[slot][2 * n_ + 1] = static_cast<unsigned>(clock64() - (t0));                        \
-      }                                                                                             \
-    }                                                                                               \
+constexpr int kTraceSlots = 5, kTraceEvents = 240;
+constexpr int kTraceBytes = kTraceSlots * kTraceEvents * 8 + 64;
+#define TRACE(slot, id, t0)                                                         \
+  do {                                                                              \
+    trace_slot = (slot);                                                            \
+    if (trace_n < kTraceEvents) {                                                   \
+      trace_buf[((slot) * kTraceEvents + trace_n) * 2] = (id);                      \
+      trace_buf[((slot) * kTraceEvents + trace_n) * 2 + 1] = (unsigned)clock();     \
+      ++trace_n;                                                                    \
+    }                                                                               \
   } while (0)
 #else
+constexpr int kTraceBytes = 0;
 #define TRACE(slot, id, t0) \
   do {                      \
   } while (0)
@@ -67,7 +70,8 @@ constexpr int kOffNorm = kOffMisc + 16;
 constexpr int kNormStride = 132;
 constexpr int kOffScaleA = kOffNorm + 2 * kNormStride * 4;
 constexpr int kOffFreq = kOffScaleA + 2 * kTileRows * 4;
-constexpr int kSmemBytes = kOffFreq + 32 * 4 + 1024;
+constexpr int kOffTrace = kOffFreq + 32 * 4;
+constexpr int kSmemBytes = kOffTrace + kTraceBytes + 1024;
 // 2 pi = kTwoPi1 + kTwoPi2 + kTwoPi3 (fp32 parts of 2 pi taken to 60 digits) and fp32(1 / (2 pi))
 constexpr float kTwoPi1 = 6.2831854820251465f, kTwoPi2 = -1.7484555314695172e-07f, kTwoPi3 = -6.8604980400235275e-15f;
 constexpr float kInvTwoPi = 0.15915493667125702f;
@@ -222,10 +226,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const long long t0 = clock64();
   (void)t0;
+#ifdef HB_TRACE
+  unsigned* trace_buf = reinterpret_cast<unsigned*>(smem + kOffTrace);
+  int trace_n = 0, trace_slot = -1;
+#endif
   const int u0 = (int)(((long long)blockIdx.x * p.units) / gridDim.x);
   const int u1 = (int)(((long long)(blockIdx.x + 1) * p.units) / gridDim.x);
   const int nunits = u1 - u0;
 
+#ifdef HB_TRACE
+  if (threadIdx.x < kTraceSlots) trace_buf[2 * kTraceSlots * kTraceEvents + threadIdx.x] = 0;
+#endif
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) {
       mbar_init(&q_full[i], kPrepWarps);
@@ -355,10 +366,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int k = 0; k < 4; ++k)
             mma_bf16_ss(tSa, smem_desc_sw128(qa + 32 * k), smem_desc_sw128(kb + 32 * k), idS, k > 0);
           tc_commit(&s_full[0]);
+          TRACE(1, 500 + kt, t0);
           if (pb_t >= 0 && !issue_pv_b()) {
             ok = false;
             break;
           }
+          TRACE(1, 600 + kt, t0);
 #pragma unroll
           for (int k = 0; k < 4; ++k)
             mma_bf16_ss(tSb, smem_desc_sw128(qd + 32 * k), smem_desc_sw128(kb + kTileBytes + 32 * k), idS, k > 0);
@@ -597,12 +610,25 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive(full_bar);
     }
   }
+#ifdef HB_TRACE
+  if (trace_slot >= 0) trace_buf[2 * kTraceSlots * kTraceEvents + trace_slot] = trace_n;
+#endif
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
+#ifdef HB_TRACE
+  if (blockIdx.x == 0) {
+    for (int i = threadIdx.x; i < kTraceSlots * kTraceEvents; i += kThreads) {
+      const int sl = i / kTraceEvents, e = i - sl * kTraceEvents;
+      g_trace[sl][2 * e] = trace_buf[2 * i];
+      g_trace[sl][2 * e + 1] = trace_buf[2 * i + 1];
+    }
+    if (threadIdx.x < kTraceSlots) g_trace_n[threadIdx.x] = trace_buf[2 * kTraceSlots * kTraceEvents + threadIdx.x];
+  }
+#endif
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
