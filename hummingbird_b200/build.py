@@ -2,8 +2,9 @@
 
     python -m hummingbird_b200.build [--verbose]
 
-One shared library, relocatable device code (the kernels share one device status word), static cudart,
-no torch types anywhere in the ABI.
+Two shared libraries, static cudart, no torch types anywhere in the ABI:
+  libhb_b200.so  the kernels (relocatable device code: they share one device status word);
+  libhb_comm.so  the NCCL exchanges of the multi-GPU paths (include/hb_comm.h), linked with libnccl.so.2.
 """
 from __future__ import annotations
 
@@ -17,6 +18,8 @@ PKG = Path(__file__).resolve().parent
 ROOT = PKG.parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libhb_b200.so"
+COMM_LIB = PKG / "libhb_comm.so"
+COMM_SOURCES = ["comm.cu"]
 SOURCES = ["abi.cu", "attn_kernel.cu", "dense_attn.cu", "band_attn.cu", "band_fused.cu", "w8a8.cu", "dit_glue.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
@@ -48,6 +51,24 @@ def build(verbose: bool = False, force: bool = False) -> Path:
     return LIB
 
 
+def build_comm(force: bool = False) -> Path:
+    """The NCCL exchange library (needs the NCCL headers and libnccl.so.2 of the CUDA image)."""
+    srcs = [CSRC / s for s in COMM_SOURCES]
+    deps = srcs + [CSRC / "hb_status.h", ROOT / "include" / "hb_comm.h"]
+    if COMM_LIB.exists() and not force and all(COMM_LIB.stat().st_mtime >= d.stat().st_mtime for d in deps):
+        return COMM_LIB
+    tmp = COMM_LIB.with_suffix(".so.tmp")
+    cmd = [nvcc(), *ARCH, "-O3", "-lineinfo", "-std=c++17", "-shared", "-Xcompiler", "-fPIC", "-I",
+           str(ROOT / "include"), "-o", str(tmp), *map(str, srcs), "-lnccl"]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f"nvcc failed ({res.returncode}):\n{res.stdout}\n{res.stderr}")
+    os.replace(tmp, COMM_LIB)
+    return COMM_LIB
+
+
 if __name__ == "__main__":
     build(verbose="--verbose" in sys.argv, force="--force" in sys.argv)
+    build_comm(force="--force" in sys.argv)
     print(LIB)
+    print(COMM_LIB)

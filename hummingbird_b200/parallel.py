@@ -90,12 +90,16 @@ def band_layout(length: int, world: int, rank: int, window: int) -> dict:
             "window": window}
 
 
-def halo_exchange(buf: torch.Tensor, layout: dict, rank: int, group=None) -> None:
+def halo_exchange(buf: torch.Tensor, layout: dict, rank: int, group=None, comm=None) -> None:
     """Fill the halo rows of `buf` (dim 1 = buffer rows, laid out as `band_layout`) from the neighbours.
 
     Rank r sends its first rows to r - 1 (that rank's trailing halo) and its last rows to r + 1 (that rank's
     leading halo), and receives its own halos the same way; all sends and receives of a rank are issued as
-    one batched group (NCCL send/recv on GPUs, gloo in the CPU tests)."""
+    one batched group. With `comm` (a `hummingbird_b200.comm.HbComm`) the exchange runs through the library's
+    NCCL C ABI; otherwise through torch.distributed (NCCL on GPUs, gloo in the CPU tests)."""
+    if comm is not None:
+        comm.halo_exchange(buf, layout)
+        return
     world, length, window = layout["world"], layout["length"], layout["window"]
     before, after = layout["before"], layout["after"]
     own0, own1 = before, layout["rows"] - after
