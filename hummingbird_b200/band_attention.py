@@ -75,3 +75,86 @@ def band_attention(qkv: torch.Tensor, q_norm, k_norm, inv_freq: torch.Tensor, nu
     length = qkv.shape[1]
     return band_attention_shard(qkv, q_norm, k_norm, inv_freq, num_heads, head_dim, window, q_begin=0,
                                 q_count=length, pos0=0, lam=lam, out=out, ws=ws)
+
+
+_STREAMS: dict[int, tuple] = {}
+
+
+def _copy_streams(device: torch.device):
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    if idx not in _STREAMS:
+        _STREAMS[idx] = (torch.cuda.Stream(device), torch.cuda.Stream(device))
+    return _STREAMS[idx]
+
+
+def band_attention_from_host(qkv_host: torch.Tensor, q_norm, k_norm, inv_freq: torch.Tensor, num_heads: int,
+                             head_dim: int, window: int, *, lam: torch.Tensor | None = None,
+                             out_host: torch.Tensor | None = None, dev_in: torch.Tensor | None = None,
+                             dev_out: torch.Tensor | None = None, layout: dict | None = None, comm=None,
+                             chunk_rows: int = 8192) -> torch.Tensor:
+    """Band attention of a projection held in pinned HOST memory, streamed through the GPU.
+
+    `qkv_host` `(B, R, 5 H 64)` bf16 pinned; the result goes to `out_host` `(B, R, H 64)` (pinned). Rows are
+    copied to the device in chunks on one copy stream; the queries of a chunk run (on the current stream) as
+    soon as their rows and the `window` rows after them have landed (whole 128-row key tiles); finished rows
+    go back on a second copy stream, so the two copy directions and the kernel overlap. Returns `out_host`;
+    the current stream is ordered after the last copy back (synchronise it before reading the result).
+
+    With `layout` (`parallel.band_layout`) and `comm` the rows are this rank's shard of a longer sequence:
+    the rows its neighbours need go first, then the halo exchange runs on the device, then the rest streams."""
+    if qkv_host.is_cuda or qkv_host.dim() != 3:
+        raise ValueError("qkv_host must be a (B, R, 5 * H * 64) host tensor")
+    device = torch.device("cuda", torch.cuda.current_device())
+    batch, own, width = qkv_host.shape
+    before = layout["before"] if layout else 0
+    after = layout["after"] if layout else 0
+    rows = before + own + after
+    out_w = num_heads * head_dim
+    if out_host is None:
+        out_host = torch.empty(batch, own, out_w, dtype=torch.bfloat16).pin_memory()
+    if dev_in is None:
+        dev_in = torch.empty(batch, rows, width, dtype=torch.bfloat16, device=device)
+    if dev_out is None:
+        dev_out = torch.empty(batch, own, out_w, dtype=torch.bfloat16, device=device)
+    qn = q_norm if isinstance(q_norm, torch.Tensor) else pack_norm(q_norm, device)
+    kn = k_norm if isinstance(k_norm, torch.Tensor) else pack_norm(k_norm, device)
+    main = torch.cuda.current_stream(device)
+    s_in, s_out = _copy_streams(device)
+    s_in.wait_stream(main)
+    s_out.wait_stream(main)
+    pos0 = layout["pos0"] if layout else 0
+    chunk = max(128, chunk_rows // 128 * 128)
+    first = [0] * batch  # own rows [0, first[b]) are already on the device
+    if layout and layout["world"] > 1:
+        # the rows the neighbours need go first (every batch element), then one halo exchange on the device
+        from hummingbird_b200 import parallel as par
+        w, rk, length, win = layout["world"], comm.rank, layout["length"], layout["window"]
+        nl = par.band_layout(length, w, rk - 1, win)["after"] if rk > 0 else 0
+        nr = par.band_layout(length, w, rk + 1, win)["before"] if rk < w - 1 else 0
+        with torch.cuda.stream(s_in):
+            for b in range(batch):
+                dev_in[b, before:before + nl].copy_(qkv_host[b, :nl], non_blocking=True)
+                dev_in[b, before + own - nr:before + own].copy_(qkv_host[b, own - nr:], non_blocking=True)
+        main.wait_stream(s_in)
+        comm.halo_exchange(dev_in, layout)
+        first = [nl] * batch
+    for b in range(batch):
+        copied = first[b]
+        for c0 in range(0, own, chunk):
+            c1 = min(own, c0 + chunk)
+            # whole key tiles up to `window` rows past the chunk (buffer coordinates), within the own rows
+            need = min(own, -(-(before + c1 + window) // 128) * 128 - before)
+            if need > copied:
+                with torch.cuda.stream(s_in):
+                    dev_in[b, before + copied:before + need].copy_(qkv_host[b, copied:need], non_blocking=True)
+                main.wait_stream(s_in)
+                copied = need
+            band_attention_shard(dev_in[b:b + 1], qn, kn, inv_freq, num_heads, head_dim, window,
+                                 q_begin=before + c0, q_count=c1 - c0, pos0=pos0, lam=lam,
+                                 out=dev_out[b:b + 1, c0:c1])
+            s_out.wait_stream(main)
+            with torch.cuda.stream(s_out):
+                out_host[b, c0:c1].copy_(dev_out[b, c0:c1], non_blocking=True)
+    main.wait_stream(s_out)
+    return out_host
+

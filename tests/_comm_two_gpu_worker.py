@@ -35,6 +35,19 @@ def main():
     full = comm.gather_pairs(local, pairs)
     torch.cuda.synchronize()
     ok &= torch.equal(full, torch.arange(pairs * 128, dtype=torch.float32, device="cuda").to(torch.bfloat16).repeat(2, 3, 1))
+    # the host-streamed API on a sequence shard (boundary rows first, halo exchange, then the rest) against
+    # the whole sequence computed on this GPU
+    from hummingbird_b200 import band_attention as hb
+    from hummingbird_b200.workloads import band_inputs
+    w = band_inputs("cuda", seed=9, length=2000, d_model=256, heads=4, window=128)
+    freqs, lam = torch.from_numpy(w.inv_freq).cuda(), torch.from_numpy(w.lam).cuda()
+    full = hb.band_attention(w.qkv, w.q_norm, w.k_norm, freqs, w.heads, 64, w.window, lam=lam)
+    lay = par.band_layout(2000, world, rank, 128)
+    host = w.qkv[:, lay["s0"]:lay["s1"]].cpu().pin_memory()
+    got = hb.band_attention_from_host(host, w.q_norm, w.k_norm, freqs, w.heads, 64, w.window, lam=lam,
+                                      layout=lay, comm=comm, chunk_rows=300)
+    torch.cuda.synchronize()
+    ok &= torch.equal(got, full[:, lay["s0"]:lay["s1"]].cpu())
     comm.close()
     flag = torch.tensor([0 if ok else 1])
     dist.all_reduce(flag)

@@ -78,3 +78,18 @@ def test_band_config2_full_length(cuda_lib):
         ref = oband.band_diff_attention(qkv[:, lo:hi], w.q_norm, w.k_norm, w.inv_freq, w.heads, w.window, lam=w.lam,
                                         offset=lo)
         check_attn(out[:, s:s + 384], ref[:, s - lo:s - lo + 384])
+
+
+def test_band_from_host_streamed_equals_device_call(cuda_lib):
+    """The host-streamed API (chunks of rows copied in, computed, copied out on overlapping streams) gives
+    the same bits as one device call, for B=2 and a chunk size that does not divide the length."""
+    from hummingbird_b200 import band_attention as hb
+    from hummingbird_b200.workloads import band_inputs
+    w = band_inputs("cuda", seed=8, batch=2, length=3000, d_model=256, heads=4, window=128)
+    freqs, lam = torch.from_numpy(w.inv_freq).cuda(), torch.from_numpy(w.lam).cuda()
+    ref = hb.band_attention(w.qkv, w.q_norm, w.k_norm, freqs, w.heads, 64, w.window, lam=lam)
+    host = w.qkv.cpu().pin_memory()
+    out = hb.band_attention_from_host(host, w.q_norm, w.k_norm, freqs, w.heads, 64, w.window, lam=lam,
+                                      chunk_rows=700)
+    torch.cuda.synchronize()
+    assert torch.equal(out, ref.cpu())
