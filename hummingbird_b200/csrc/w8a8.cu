@@ -333,6 +333,222 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
 }
 
+// ------------------------------------------------------------------ GEMM on CTA pairs (cta_group::2)
+// A cluster of two CTAs on neighbouring SMs computes a 256 x BN tile with one pair MMA stream: each CTA
+// holds 128 rows of A and BN / 2 rows of W per stage, so every SM loads half the B bytes of the one-CTA
+// kernel for the same MMA work. The even CTA's warp 1 issues `tcgen05.mma.cta_group::2`; each CTA's TMEM
+// receives its own 128 rows of the accumulator and its epilogue warps convert and store them. Stage
+// completion bytes of both CTAs count on the even CTA's `full` barrier; the pair MMA thread commits each
+// stage and each accumulator to the barriers of both CTAs; both CTAs' epilogues release an accumulator on
+// the even CTA's `acc_empty`. No TMA load uses multicast.
+template <int BN>
+struct PairCfg {
+  static constexpr int kBHalf = BN / 2;
+  static constexpr int kStages = BN == 256 ? 4 : 6;
+  static constexpr int kABytes = kBM * kBK;
+  static constexpr int kBBytes = kBHalf * kBK;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kOffOut = kStages * kStageBytes;
+  static constexpr int kOutBytes = kBM * BN * 2;
+  static constexpr int kOffParams = kOffOut + kOutBytes;
+  static constexpr int kOffBars = kOffParams + 2 * 2 * BN * 4;
+  static constexpr int kNumBars = 2 * kStages + 2 + 2 + 1;  // full, empty, acc_full, acc_empty, drain
+  static constexpr int kSmem = kOffBars + kNumBars * 8 + 16 + 1024;
+  static constexpr uint32_t kTmemCols = 2 * BN;
+};
+
+template <int BN>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    w8a8_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                          const __grid_constant__ CUtensorMap tmap_out, const GemmEpi e) {
+  using C = PairCfg<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
+  float* params = reinterpret_cast<float*>(smem + C::kOffParams);
+  uint64_t* bar_full = reinterpret_cast<uint64_t*>(smem + C::kOffBars);
+  uint64_t* bar_empty = bar_full + C::kStages;
+  uint64_t* acc_full = bar_empty + C::kStages;  // [2]
+  uint64_t* acc_empty = acc_full + 2;           // [2] used in the even CTA: 2 x 8 epilogue warps
+  uint64_t* drain = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const uint32_t peer = rank ^ 1u;
+  const int cluster = blockIdx.x >> 1, clusters = gridDim.x >> 1;
+  const int num_m = (e.M + 2 * kBM - 1) / (2 * kBM), num_n = (e.N + BN - 1) / BN;
+  const int tiles = num_m * num_n;
+  const int nk = (e.K + kBK - 1) / kBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(&bar_full[s], 1);
+      mbar_init(&bar_empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 2 * (kEpiThreads / 32));
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    prefetch_tmap(&tmap_a);
+    prefetch_tmap(&tmap_b);
+    prefetch_tmap(&tmap_out);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, C::kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // both CTAs' barriers are initialised before any cross-CTA arrival
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- TMA producer (both CTAs)
+    if (lane == 0) {
+      int it = 0;
+      for (int tile = cluster; tile < tiles && !*abort_flag; tile += clusters) {
+        const int m0 = (tile % num_m) * 2 * kBM + static_cast<int>(rank) * kBM;
+        const int nb = (tile / num_m) * BN + static_cast<int>(rank) * C::kBHalf;
+        for (int i = 0; i < nk; ++i, ++it) {
+          const int st = it % C::kStages;
+          if (it >= C::kStages && !mbar_wait(&bar_empty[st], ((it / C::kStages) & 1) ^ 1)) {
+            *abort_flag = 1;
+            break;
+          }
+          uint8_t* sa = smem + st * C::kStageBytes;
+          const uint32_t full0 = cluster_addr(smem_u32(&bar_full[st]), 0);
+          if (rank == 0) mbar_arrive_expect_tx(&bar_full[st], 2 * C::kStageBytes);
+          tma_load_2d_pair(sa, &tmap_a, i * kBK, m0, full0);
+          tma_load_2d_pair(sa + C::kABytes, &tmap_b, i * kBK, nb, full0);
+        }
+      }
+      // every copy into this CTA's shared memory has landed before it exits: the even CTA's full barrier
+      // completes only when both CTAs' bytes of a stage arrived, and the final cluster barrier below waits
+      // for the even CTA, whose MMA thread consumed every stage
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- pair MMA issuer (even CTA)
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t idesc = idesc_s8_s32(2 * kBM, BN);
+      bool ok = true;
+      int it = 0, local = 0;
+      for (int tile = cluster; ok && tile < tiles; tile += clusters, ++local) {
+        const int a = local & 1;
+        if (local >= 2 && !mbar_wait(&acc_empty[a], ((local >> 1) & 1) ^ 1)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t acc = tmem + a * BN;
+        for (int i = 0; i < nk; ++i, ++it) {
+          const int st = it % C::kStages;
+          if (!mbar_wait(&bar_full[st], (it / C::kStages) & 1) || *abort_flag) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + st * C::kStageBytes);
+          const uint32_t sb = sa + C::kABytes;
+#pragma unroll
+          for (int k = 0; k < kBK / 32; ++k)
+            mma_i8_ss_pair(acc, smem_desc_sw128(sa + 32 * k), smem_desc_sw128(sb + 32 * k), idesc, (i > 0 || k > 0));
+          const uint32_t eb = smem_u32(&bar_empty[st]);
+          tc_commit_pair(cluster_addr(eb, 0));
+          tc_commit_pair(cluster_addr(eb, 1));
+        }
+        if (ok) {
+          const uint32_t fb = smem_u32(&acc_full[a]);
+          tc_commit_pair(cluster_addr(fb, 0));
+          tc_commit_pair(cluster_addr(fb, 1));
+        }
+      }
+      if (!ok) *abort_flag = 1;
+      tc_commit_pair(cluster_addr(smem_u32(drain), 0));
+      mbar_wait(drain, 0);
+    }
+  } else {
+    // ---------------------------------------------------------------- epilogue: warps 2..9 of both CTAs
+    const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const int et = threadIdx.x - 64;
+    const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
+    int local = 0;
+    for (int tile = cluster; tile < tiles; tile += clusters, ++local) {
+      const int a = local & 1;
+      const int m0 = (tile % num_m) * 2 * kBM + static_cast<int>(rank) * kBM, n0 = (tile / num_m) * BN;
+      if (et == 0 && local > 0) bulk_wait_group_read0();
+      float* psw = params + (local & 1) * 2 * BN;
+      float* pbias = psw + BN;
+      for (int c = et; c < BN; c += kEpiThreads) {
+        const int n = n0 + c;
+        psw[c] = n < e.N ? e.sw[n] : 0.f;
+        pbias[c] = (e.bias && n < e.N) ? __uint_as_float(static_cast<uint32_t>(e.bias[n]) << 16) : 0.f;
+      }
+      asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory");
+      const bool ok = __all_sync(0xffffffffu, mbar_wait(&acc_full[a], (local >> 1) & 1));
+      if (!ok) break;
+      tc_fence_after();
+      const int r = quad * 32 + lane;
+      const int m = m0 + r;
+      const float sxm = m < e.M ? e.sx[m] : 0.f;
+      const uint32_t taddr = tmem + lane_base + a * BN;
+      uint8_t* stage_out = smem + C::kOffOut;
+#pragma unroll 1
+      for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
+        uint32_t acc[32];
+        tmem_ld32(taddr + 32 * c, acc);
+        tmem_wait_ld();
+        uint32_t w[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          float y[2];
+#pragma unroll
+          for (int t = 0; t < 2; ++t) {
+            const int cc = 32 * c + 2 * j + t;
+            float v = __fmul_rn(__int2float_rn(static_cast<int>(acc[2 * j + t])), sxm);
+            v = __fmul_rn(v, psw[cc]);
+            y[t] = __fadd_rn(v, pbias[cc]);
+          }
+          w[j] = pack_bf16x2(y[0], y[1]);
+        }
+        uint8_t* box = stage_out + (c >> 1) * (kBM * 128);
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          *reinterpret_cast<uint4*>(box + sw128_offset(r, (c & 1) * 4 + j)) =
+              make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+        if (e.acc_out && m < e.M && n0 + 32 * c < e.N) {
+          uint4* a4 = reinterpret_cast<uint4*>(e.acc_out + (size_t)m * e.ldacc + n0 + 32 * c);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) a4[j] = make_uint4(acc[4 * j], acc[4 * j + 1], acc[4 * j + 2], acc[4 * j + 3]);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(cluster_addr(smem_u32(&acc_empty[a]), 0));
+      fence_proxy_async_smem();
+      asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory");
+      if (et == 0) {
+#pragma unroll 1
+        for (int bx = 0; bx < BN / 64; ++bx)
+          if (n0 + 64 * bx < e.N && m0 < e.M) tma_store_2d(&tmap_out, n0 + 64 * bx, m0, stage_out + bx * (kBM * 128));
+        bulk_commit_group();
+      }
+    }
+    if (et == 0) bulk_wait_group0();
+  }
+  tc_fence_before();
+  cluster_sync();  // no CTA leaves while its peer may still signal its barriers or read its shared memory
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, C::kTmemCols);
+  }
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   if (!fn) {
@@ -392,6 +608,38 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap&
   return cudaGetLastError() == cudaSuccess ? HB_OK : HB_ERR_LAUNCH;
 }
 
+template <int BN>
+int launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to, const GemmEpi& e,
+                     cudaStream_t stream) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return HB_ERR_LAUNCH;
+  static bool configured[64] = {};
+  if (dev < 64 && !configured[dev]) {
+    if (cudaFuncSetAttribute(w8a8_gemm_pair_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             PairCfg<BN>::kSmem) != cudaSuccess)
+      return HB_ERR_LAUNCH;
+    configured[dev] = true;
+  }
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int tiles = ((e.M + 2 * kBM - 1) / (2 * kBM)) * ((e.N + BN - 1) / BN);
+  const int clusters = tiles < sms / 2 ? tiles : sms / 2;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * clusters, 1, 1);
+  cfg.blockDim = dim3(kGemmThreads, 1, 1);
+  cfg.dynamicSmemBytes = PairCfg<BN>::kSmem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, w8a8_gemm_pair_kernel<BN>, ta, tb, to, e) != cudaSuccess) return HB_ERR_LAUNCH;
+  return cudaGetLastError() == cudaSuccess ? HB_OK : HB_ERR_LAUNCH;
+}
+
 }  // namespace
 }  // namespace hb
 
@@ -420,10 +668,18 @@ extern "C" int hb_w8a8_gemm(const void* qx, int64_t ldqx, const float* sx, const
   int st = check_device();
   if (st != HB_OK) return st;
   GemmEpi e{sx, sw, static_cast<const uint16_t*>(bias), static_cast<uint16_t*>(out), ldo, acc_out, ldacc, M, N, K};
-  const bool wide = (N % 256 == 0) && ((long)((M + kBM - 1) / kBM) * (N / 256) >= 148);
   CUtensorMap ta, tb, to;
   if (!make_tmap_i8(&ta, qx, M, K, ldqx, kBM)) return HB_ERR_LAUNCH;
-  if (!make_tmap_i8(&tb, qw, N, K, ldqw, wide ? 256 : 128)) return HB_ERR_LAUNCH;
   if (!make_tmap_out(&to, out, M, N, ldo)) return HB_ERR_LAUNCH;
+  // CTA pairs (256-row tiles, half the weight bytes per SM) pay off on long K: measured at 8192^3 2,911 vs
+  // 2,557 TOPS; at the DiT / config-3 shapes (K <= 4096, two to nine waves) the one-CTA kernel is as fast
+  // or faster (e.g. 5296 x 1024 x 8192: 53.2 vs 55.3 us), so it keeps those.
+  if (M >= 8 * kBM && K >= 8192) {
+    const bool wide = (N % 256 == 0) && ((long)((M + 2 * kBM - 1) / (2 * kBM)) * (N / 256) >= 74);
+    if (!make_tmap_i8(&tb, qw, N, K, ldqw, wide ? 128 : 64)) return HB_ERR_LAUNCH;
+    return wide ? launch_gemm_pair<256>(ta, tb, to, e, stream) : launch_gemm_pair<128>(ta, tb, to, e, stream);
+  }
+  const bool wide = (N % 256 == 0) && ((long)((M + kBM - 1) / kBM) * (N / 256) >= 148);
+  if (!make_tmap_i8(&tb, qw, N, K, ldqw, wide ? 256 : 128)) return HB_ERR_LAUNCH;
   return wide ? launch_gemm<256>(ta, tb, to, e, stream) : launch_gemm<128>(ta, tb, to, e, stream);
 }

@@ -1,5 +1,6 @@
 """GPU parity for the W8A8 path through the C ABI: quantisation, int32 accumulators and the bf16 epilogue are
-all bit-exact against the CPU oracle (oracle/w8a8.py)."""
+all bit-exact against the CPU oracle (oracle/w8a8.py). Shapes with K >= 8192 and M >= 1024 run the CTA-pair
+kernel (ragged M, N and K included); the others the one-CTA kernel."""
 import numpy as np
 import pytest
 import torch
@@ -32,7 +33,8 @@ def test_w8a8_golden_bit_exact(cuda_lib):
     assert np.array_equal(bits_np(y)[:, :12], z["y_bits"])
 
 
-@pytest.mark.parametrize("m,k,n", [(2584, 1024, 4096), (2584, 4096, 1024), (200, 272, 96), (1, 16, 32)])
+@pytest.mark.parametrize("m,k,n", [(2584, 1024, 4096), (2584, 4096, 1024), (1100, 8192, 1024), (1030, 8208, 352),
+                                   (513, 272, 96), (200, 272, 96), (1, 16, 32)])
 def test_w8a8_gemm_bit_exact(m, k, n, cuda_lib):
     from hummingbird_b200.w8a8 import quantize_rows, w8a8_gemm
     g = torch.Generator(device="cuda").manual_seed(m * 7 + k * 3 + n)
