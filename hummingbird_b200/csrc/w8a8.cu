@@ -376,7 +376,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();
-  const uint32_t peer = rank ^ 1u;
   const int cluster = blockIdx.x >> 1, clusters = gridDim.x >> 1;
   const int num_m = (e.M + 2 * kBM - 1) / (2 * kBM), num_n = (e.N + BN - 1) / BN;
   const int tiles = num_m * num_n;

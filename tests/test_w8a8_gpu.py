@@ -34,7 +34,7 @@ def test_w8a8_golden_bit_exact(cuda_lib):
 
 
 @pytest.mark.parametrize("m,k,n", [(2584, 1024, 4096), (2584, 4096, 1024), (1100, 8192, 1024), (1030, 8208, 352),
-                                   (513, 272, 96), (200, 272, 96), (1, 16, 32)])
+                                   (1300, 512, 1024), (513, 272, 96), (200, 272, 96), (1, 16, 32)])
 def test_w8a8_gemm_bit_exact(m, k, n, cuda_lib):
     from hummingbird_b200.w8a8 import quantize_rows, w8a8_gemm
     g = torch.Generator(device="cuda").manual_seed(m * 7 + k * 3 + n)
