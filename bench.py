@@ -245,6 +245,28 @@ def time_band_e2e(step: BandStep, steps: int, warmup: int, world: int) -> dict:
 
 
 # ----------------------------------------------------------------------------------------------- dense
+def _event_median(fn, steps: int, warmup: int, flush) -> float:
+    """Median CUDA-event time of `fn` on the current stream, L2 flushed before each call. A ~50 us GPU sleep
+    between the flush and the start event keeps the GPU busy while the host enqueues the call, so the
+    interval holds the device work of `fn` and not the host's launch latency."""
+    import torch
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    times = []
+    stream = torch.cuda.current_stream()
+    for _ in range(steps):
+        flush.zero_()
+        torch.cuda._sleep(100_000)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        fn()
+        b.record(stream)
+        times.append((a, b))
+    torch.cuda.synchronize()
+    return statistics.median(a.elapsed_time(b) for a, b in times)
+
+
 def time_dense(device, steps: int, warmup: int, batch: int, length: int, heads: int, d_model: int) -> dict:
     import torch
     from hummingbird_b200 import dense_attention as hb
@@ -259,23 +281,45 @@ def time_dense(device, steps: int, warmup: int, batch: int, length: int, heads: 
     def one():
         hb.dense_attention(w.qkv, qw, kw, cos, sin, mask, heads, 64, w.half, w.eps, lam=lam, out=out)
 
-    for _ in range(warmup):
-        one()
-    torch.cuda.synchronize()
-    times = []
-    stream = torch.cuda.current_stream()
-    for _ in range(steps):
-        flush.zero_()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record(stream)
-        one()
-        b.record(stream)
-        times.append((a, b))
-    torch.cuda.synchronize()
-    ms = statistics.median(a.elapsed_time(b) for a, b in times)
+    ms = _event_median(one, steps, warmup, flush)
     flops = 8.0 * batch * heads * length * length * 64
     return {"config": {"batch": batch, "length": length, "heads": heads}, "ms": ms,
             "tflops": flops / (ms * 1e-3) / 1e12, "launches_per_call": 2, "l2": "flushed (256 MB write) before each call"}
+
+
+def time_cross(device, steps: int, warmup: int, hbm_peak: float, batch: int = 2, length: int = 2648,
+               heads: int = 16, context: int = 128) -> dict:
+    """The DiT's differential cross-attention per block call (120 s clip shape): this library's kernel against
+    the torch ops it replaces in the DiT (q RMSNorm, two cuDNN/flash SDPA calls, subtraction, head merge)."""
+    import torch
+    import torch.nn.functional as F
+    from hummingbird_b200.cross_attention import cross_attention, cross_kv
+    g = torch.Generator(device=device).manual_seed(7)
+    width = heads * 64
+    q2 = torch.randn(batch, length, 2 * width, generator=g, device=device).to(torch.bfloat16)
+    kv = cross_kv(torch.randn(batch, context, 3 * width, generator=g, device=device).to(torch.bfloat16),
+                  1 + 0.02 * torch.randn(64, generator=g, device=device), heads, 1e-6)
+    qw = (1 + 0.02 * torch.randn(64, generator=g, device=device)).to(torch.bfloat16)
+    out = torch.empty(batch, length, width, dtype=torch.bfloat16, device=device)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)  # > L2 (126 MB)
+    qwf = qw.float()
+    ms = _event_median(lambda: cross_attention(q2, kv, qwf, None, heads, 64, 1e-6, out=out), steps, warmup, flush)
+    k, kd, v = (t.unflatten(-1, (heads, 64)).transpose(1, 2) for t in kv.chunk(3, -1))
+
+    def torch_ops():
+        q = F.rms_norm(q2.view(batch, length, 2, heads, 64), (64,), qw, 1e-6)
+        a, b = q[:, :, 0].transpose(1, 2), q[:, :, 1].transpose(1, 2)
+        o = F.scaled_dot_product_attention(a, k, v) - F.scaled_dot_product_attention(b, kd, v)
+        return o.transpose(1, 2).reshape(batch, length, width)
+
+    ms_torch = _event_median(torch_ops, steps, warmup, flush)
+    nbytes = 2 * (batch * length * 2 * width + batch * context * 3 * width + batch * length * width)
+    flops = 8.0 * batch * heads * length * context * 64
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    return {"config": {"batch": batch, "q_len": length, "kv_len": context, "heads": heads}, "ms": ms,
+            "gbs": gbs, "hbm_frac": gbs / hbm_peak, "tflops": flops / (ms * 1e-3) / 1e12,
+            "algorithmic_bytes": nbytes, "launches_per_call": 1, "torch_ops_ms": ms_torch,
+            "l2": "flushed (256 MB write) before each call"}
 
 
 # ----------------------------------------------------------------------------------------------- w8a8
@@ -676,6 +720,7 @@ def main():
         if world == 1:
             paths["dense_config1"] = time_dense(device, 50, 5, 1, 646, 16, 1024)
             paths["dense_120s_block_call"] = time_dense(device, 20, 3, 2, 2648, 16, 1024)
+            paths["cross_120s_block_call"] = time_cross(device, 50, 5, peaks["hbm_gbs"])
             paths["w8a8_config3"] = time_w8a8(device, 50, 5)
             paths["dit_120s_clip_bf16_mlp"] = time_dit_clip(device, "none")
         paths["dit_120s_clip_w8a8_mlp"] = time_dit_clip(device, "w8a8", world)

@@ -29,6 +29,7 @@ SIGNATURES: dict[str, list] = {
     "hb_dense_noalloc_max_bytes": [C.POINTER(_sz)],
     "hb_dense_diff_attn_noalloc": [_p, _i64, _p, _p, _p, _p, _i64, _p, _i64, _i64, _p, _p, _i64, _i, _i, _i, _i, _i,
                                    _f, _i, _i, _p],
+    "hb_cross_diff_attn": [_p, _i64, _p, _i64, _p, _p, _p, _p, _i64, _i, _i, _i, _i, _i, _f, _p],
     "hb_band_workspace_bytes": [_i, _i, _i, _i, _i, C.POINTER(_sz)],
     "hb_band_diff_attn": [_p, _i64, _p, _p, _p, _i, _p, _p, _i64, _i, _i, _i, _i, _i64, _i, _i, _i, _i, _i, _p, _sz,
                           _i, _p],

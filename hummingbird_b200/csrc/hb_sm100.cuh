@@ -100,6 +100,12 @@ __device__ __forceinline__ void tma_store_2d(const void* tmap, int c0, int c1, c
   asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%1, %2}], [%3];"
                ::"l"(tmap), "r"(c0), "r"(c1), "r"(smem_u32(src)) : "memory");
 }
+// 3-D tiled tensor store shared -> global (bulk group); coordinates innermost first, out-of-range parts of the
+// box are not written.
+__device__ __forceinline__ void tma_store_3d(const void* tmap, int c0, int c1, int c2, const void* src) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%1, %2, %3}], [%4];"
+               ::"l"(tmap), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(src)) : "memory");
+}
 __device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // wait until the shared-memory sources of all committed bulk stores of this thread may be overwritten
 __device__ __forceinline__ void bulk_wait_group_read0() {

@@ -3,9 +3,11 @@
 Used to time a whole 120 s clip (the benchmark's config 4): `sa3jax.sampling.pingpong` (sampling.py:81-118)
 over `sa3jax.dit.dit_forward` (dit.py:340-361) with its 24 `_block`s (dit.py:224-250). The self-attention is
 this library's fused differential kernel (`blocks.dit_self_attention`'s path); the MLP is W8A8 when
-`DiTConfig.ff_quant == "w8a8"` (else a bf16 matmul); projections, RMSNorm / adaLN elementwise work and the
-differential cross-attention over the 128 hoisted context tokens (dit.py:203-215, 274-284) run as torch ops
-(cuBLAS / cuDNN-flash library kernels). No checkpoint is loaded: weights are N(0, 1 / fan_in) bf16 draws.
+`DiTConfig.ff_quant == "w8a8"` (else a bf16 matmul); with `glue="cuda"` the differential cross-attention over
+the 128 hoisted context tokens (dit.py:203-215, 274-284) is this library's `hb_cross_diff_attn` kernel and the
+residual / RMSNorm / adaLN / GLU steps its row kernels; projections are torch matmuls (cuBLAS). With
+`glue="torch"` the cross-attention and the elementwise steps run as torch ops (cuDNN-flash SDPA). No checkpoint
+is loaded: weights are N(0, 1 / fan_in) bf16 draws.
 
 With a process group of N ranks (one per GPU) one clip runs on all N: token-wise work is split by token rows
 and the self-attention by head pairs, with two all-to-alls per block (`hummingbird_b200.parallel`); each rank
@@ -24,6 +26,7 @@ import torch
 import torch.distributed as dist
 import torch.nn.functional as F
 
+from hummingbird_b200 import cross_attention as hb_cross
 from hummingbird_b200 import dense_attention as hb_dense
 from hummingbird_b200 import dit_glue as glue
 from hummingbird_b200 import parallel as par
@@ -122,6 +125,7 @@ class DiT:
             for name in ("pre_norm", "cross_attend_norm", "ff_norm"):
                 b[name + "_bf"] = b[name].to(torch.bfloat16)  # checkpoint norm weights are bf16
             b["cross_attn"]["q_norm_bf"] = b["cross_attn"]["q_norm"].to(torch.bfloat16)
+            b["cross_attn"]["q_norm_f"] = b["cross_attn"]["q_norm_bf"].float()
             if self.world > 1:  # rows grouped by destination rank: one batched GEMM fills the all-to-all buffer
                 rows = par.dest_major_qkv_rows(h, self.world).to(device)
                 b["self_attn"]["to_qkv_dest"] = b["self_attn"]["to_qkv"][rows].view(self.world, -1, d).transpose(1, 2)
@@ -138,13 +142,16 @@ class DiT:
         valid = torch.ones(self.shape.batch, seq, device=self.device)
         cos, sin, mask = hb_dense.tables(seq, self.p["rope_inv_freq"], valid, cfg.head_dim)
         ctx = self._seq(self.p["to_cond_embed"], cross_cond.to(torch.bfloat16))
-        kv = []
+        kv, kv_rows = [], []
         for b in self.blocks:
             x = ctx @ b["cross_attn"]["to_kv"].T
-            k, kd, v = (t.unflatten(-1, (h, cfg.head_dim)).transpose(1, 2) for t in x.chunk(3, -1))
             kn = b["cross_attn"]["k_norm"]
+            if self.glue == "cuda":  # the kernel's layout: (B, context, [k | k_diff | v]) rows, keys k-normed
+                kv_rows.append(hb_cross.cross_kv(x, kn, h, cfg.qk_norm_eps, cfg.head_dim))
+                continue
+            k, kd, v = (t.unflatten(-1, (h, cfg.head_dim)).transpose(1, 2) for t in x.chunk(3, -1))
             kv.append((_rms(k, kn, cfg.qk_norm_eps), _rms(kd, kn, cfg.qk_norm_eps), v))
-        return {"lane_cos": cos, "lane_sin": sin, "lane_mask": mask, "cross_kv": kv,
+        return {"lane_cos": cos, "lane_sin": sin, "lane_mask": mask, "cross_kv": kv, "cross_kv_rows": kv_rows,
                 "gcond_proj": self._seq(self.p["to_global_embed"], global_cond.to(torch.bfloat16))}
 
     @staticmethod
@@ -223,7 +230,7 @@ class DiT:
             c = conds[i]
             y = self._self_attn(x, b["self_attn"], static) @ b["self_attn"]["to_out"].T
             x = glue.residual_norm(h, y=y, gate=part(c, 2), weight=b["cross_attend_norm_bf"], eps=eps)
-            y = self._cross(x, b["cross_attn"], static["cross_kv"][i])
+            y = self._cross_fused(x, b["cross_attn"], static["cross_kv_rows"][i])
             x = glue.residual_norm(h, y=y, local=b["local"], local_row0=self.mem_rows, weight=b["ff_norm_bf"],
                                    scale=part(c, 3), shift=part(c, 4), eps=eps)
             y = self._ff(x, b)
@@ -250,16 +257,20 @@ class DiT:
         att = self.attend(qkv, *args, cfg.num_heads // self.world, cfg.head_dim, cfg.rope_dim // 2, cfg.qk_norm_eps)
         return par.pairs_to_tokens(att, self.seq, self.world, self.rank, self.group)
 
+    def _cross_fused(self, x, ca, kv_rows):
+        """Differential cross-attention (dit.py:203-215) as this library's kernel: `to_q`, then q RMSNorm and
+        both softmax branches over the hoisted keys in one launch (`hb_cross_diff_attn`), then `to_out`."""
+        cfg = self.cfg
+        att = hb_cross.cross_attention(x @ ca["to_q"].T, kv_rows, ca["q_norm_f"], None, cfg.num_heads,
+                                       cfg.head_dim, cfg.qk_norm_eps)
+        return att @ ca["to_out"].T
+
     def _cross(self, x, ca, kv):
-        """Differential cross-attention, no RoPE, no mask (dit.py:203-215): SDPA(q) - SDPA(q_diff)."""
+        """Differential cross-attention, no RoPE, no mask (dit.py:203-215): SDPA(q) - SDPA(q_diff), torch ops."""
         cfg = self.cfg
         bsz, length, _ = x.shape
-        q2 = x @ ca["to_q"].T
-        if self.glue == "cuda":
-            q2 = glue.head_rms_norm(q2, ca["q_norm_bf"], cfg.qk_norm_eps)
-        q2 = q2.view(bsz, length, 2, cfg.num_heads, cfg.head_dim)
-        if self.glue == "torch":
-            q2 = F.rms_norm(q2, (cfg.head_dim,), ca["q_norm_bf"], cfg.qk_norm_eps)
+        q2 = (x @ ca["to_q"].T).view(bsz, length, 2, cfg.num_heads, cfg.head_dim)
+        q2 = F.rms_norm(q2, (cfg.head_dim,), ca["q_norm_bf"], cfg.qk_norm_eps)
         q, qd = q2[:, :, 0].transpose(1, 2), q2[:, :, 1].transpose(1, 2)
         k, kd, v = kv
         out = F.scaled_dot_product_attention(q, k, v) - F.scaled_dot_product_attention(qd, kd, v)

@@ -81,6 +81,25 @@ int hb_dense_diff_attn_noalloc(const void* qkv, int64_t qkv_row_stride, const fl
                                int64_t out_row_stride, int batch, int length, int num_heads, int head_dim, int half,
                                float eps, int pair_begin, int pair_count, cudaStream_t stream);
 
+/* ---- differential cross-attention (DiT) ------------------------------------------------------------- */
+/* Replaces the attention of `sa3jax.dit._cross_attention` (dit.py:203-215): `_attend` with no RoPE and no
+ * mask (dit.py:150-176) and `_attend_out`'s `SDPA(q, k, v) - SDPA(q_diff, k_diff, v)` (dit.py:131-147), up to
+ * (not including) `to_out`. The reference runs it as XLA ops; this is one kernel:
+ *   q         bf16 [batch, q_len, q_row_stride]: the `to_q` output, columns [q | q_diff], each num_heads * 64.
+ *   kv        bf16 [batch, kv_len, kv_row_stride]: the hoisted `to_kv` output (dit.py:274-284), columns
+ *             [k | k_diff | v], each num_heads * 64; kv_len <= 384.
+ *   q_weight  fp32 [64] q RMSNorm scale (applied to q and q_diff, dit.py:167-169).
+ *   k_weight  fp32 [64] k RMSNorm scale applied to k and k_diff here, or NULL when kv already holds the
+ *             k-normed keys (the reference hoists the norm, dit.py:122-128, 283).
+ *   lam       fp32 [num_heads / 2] per-pair lambda of `A - lambda * B`, or NULL for lambda = 1 (the reference).
+ *   out       bf16; row (b, l) at out + (b * q_len + l) * out_row_stride, head h at column h * 64.
+ * Scores are q k^T / 8 in fp32; softmax in fp32 with bf16 weights into P V, normalised after P V; each branch
+ * normalised, then one fp32 subtraction and one bf16 cast. head_dim must be 64; rows 16-byte aligned. */
+int hb_cross_diff_attn(const void* q, int64_t q_row_stride, const void* kv, int64_t kv_row_stride,
+                       const float* q_weight, const float* k_weight, const float* lam, void* out,
+                       int64_t out_row_stride, int batch, int q_len, int kv_len, int num_heads, int head_dim,
+                       float eps, cudaStream_t stream);
+
 /* ---- band (sliding-window) differential attention (SAME-L decoder) --------------------------------- */
 /* Bytes of workspace hb_band_diff_attn needs for `rows` buffer rows, `pair_count` head pairs, `window` and
  * rotate-half width `half`: a rows x half (cos, sin) table for window <= 128 (the fused kernel), prepared

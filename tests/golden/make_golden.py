@@ -12,6 +12,8 @@ reference checkout (default `/root/reference`, or `$HB_REFERENCE`). The referenc
 * band: `sa3jax.same_l._attention` (same_l.py:151-169) with `SameConfig(attention="xla")`,
   `stride = window - 1`, mask from `same_l._swa_mask`; branches A and B through `same_l._rope`,
   `_dyt` and `_sdpa` composed as `_attention` composes them (same_l.py:162-168).
+* cross: `sa3jax.dit._cross_attention` (dit.py:203-215) over keys hoisted by `sa3jax.dit._cross_kv`
+  (dit.py:274-284), identity `to_q` / `to_kv` / `to_out`; branches A and B with `differential=False`.
 * w8a8: no reference exists; the accumulators come from a pure-Python integer dot product, independent
   of the numpy oracle.
 
@@ -85,6 +87,41 @@ def dense_case(name, *, seed, batch, length, heads, half, w_scale=1.0, masked_ta
     print(f"{name}: out absmax {np.abs(out).max():.4f}")
 
 
+def cross_case(name, *, seed, batch, q_len, kv_len, heads, w_scale=1.0):
+    """`sa3jax.dit._cross_attention` (dit.py:203-215) on K/V hoisted by `sa3jax.dit._cross_kv` (dit.py:274-284),
+    identity `to_q` / `to_kv` / `to_out`; branches A and B through the same function with `differential=False`."""
+    config, dit, dtypes, _ = _import_reference()
+    rng = np.random.default_rng(seed)
+    inner = heads * 64
+    q_bits, q2 = _bf16(rng.standard_normal((batch, q_len, 2 * inner)))
+    kv_bits, kv = _bf16(rng.standard_normal((batch, kv_len, 3 * inner)))
+    q_w = (w_scale + 0.02 * rng.standard_normal(64)).astype(np.float32)
+    k_w = (w_scale + 0.02 * rng.standard_normal(64)).astype(np.float32)
+    lam = rng.uniform(0.2, 0.8, heads // 2).astype(np.float32)
+    f32 = dtypes.FP32_PARITY
+
+    def run(q_in, kv_in, differential):
+        cfg = config.DiTConfig(embed_dim=inner, num_heads=heads, differential=differential, attention="xla")
+        block = {"cross_attn": {"to_q": {"weight": np.eye(q_in.shape[-1], dtype=np.float32)},
+                                "to_kv": {"weight": np.eye(kv_in.shape[-1], dtype=np.float32)},
+                                "q_norm": {"weight": q_w}, "k_norm": {"weight": k_w},
+                                "to_out": {"weight": np.eye(inner, dtype=np.float32)}}}
+        hoisted = dit._cross_kv(block, kv_in.astype(np.float32), cfg, f32)
+        static = {"cross_k": [hoisted[0]], "cross_v": [hoisted[-1]]}
+        if differential:
+            static["cross_k_diff"] = [hoisted[1]]
+        return dit._cross_attention(q_in.astype(np.float32), static, block, 0, cfg, f32)
+
+    out = run(q2, kv, True)
+    qs, kvs = np.split(q2, 2, axis=-1), np.split(kv, 3, axis=-1)
+    branch_a = run(qs[0], np.concatenate([kvs[0], kvs[2]], -1), False)
+    branch_b = run(qs[1], np.concatenate([kvs[1], kvs[2]], -1), False)
+    np.savez_compressed(HERE / f"{name}.npz", q_bits=q_bits, kv_bits=kv_bits, q_weight=q_w, k_weight=k_w, lam=lam,
+                        heads=heads, eps=np.float32(1e-6), out_ref=out.astype(np.float32),
+                        branch_a=branch_a.astype(np.float32), branch_b=branch_b.astype(np.float32))
+    print(f"{name}: out absmax {np.abs(out).max():.4f}")
+
+
 def band_case(name, *, seed, batch, length, heads, half, window, alpha=0.5, gamma=1.0):
     config, _, dtypes, same_l = _import_reference()
     rng = np.random.default_rng(seed)
@@ -151,6 +188,8 @@ def main():
     dense_case("dense_h4_l200_full", seed=10, batch=2, length=200, heads=4, half=32, masked_tail=40)
     dense_case("dense_h2_l130_partial", seed=11, batch=1, length=130, heads=2, half=16)
     dense_case("dense_h2_l257_sharp", seed=12, batch=1, length=257, heads=2, half=32, w_scale=3.0)
+    cross_case("cross_h4_q200_kv128", seed=40, batch=2, q_len=200, kv_len=128, heads=4)
+    cross_case("cross_h2_q130_kv257_sharp", seed=41, batch=1, q_len=130, kv_len=257, heads=2, w_scale=3.0)
     band_case("band_w17_l204_partial", seed=20, batch=1, length=204, heads=4, half=16, window=17)
     band_case("band_w128_l384_full", seed=21, batch=1, length=384, heads=2, half=32, window=128)
     band_case("band_w17_l136_sharp", seed=22, batch=1, length=136, heads=2, half=16, window=17, alpha=1.5,

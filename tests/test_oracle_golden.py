@@ -5,11 +5,12 @@ import numpy as np
 import pytest
 
 from conftest import load_golden
-from oracle import band, dense, w8a8
+from oracle import band, cross, dense, w8a8
 from oracle.common import bf16_bits_to_f32, check_close
 
 DENSE = ["dense_h4_l200_full", "dense_h2_l130_partial", "dense_h2_l257_sharp"]
 BAND = ["band_w17_l204_partial", "band_w128_l384_full", "band_w17_l136_sharp"]
+CROSS = ["cross_h4_q200_kv128", "cross_h2_q130_kv257_sharp"]
 
 
 def _band_norms(z):
@@ -32,6 +33,40 @@ def test_dense_oracle_matches_reference(name):
     lam = z["lam"]
     ref = z["branch_a"] - np.repeat(lam, 128)[None, None, :] * z["branch_b"]
     check_close(dense.dense_diff_attention(*args, lam=lam), ref, max_abs=1e-5, mean_abs=1e-6)
+
+
+@pytest.mark.parametrize("name", CROSS)
+def test_cross_oracle_matches_reference(name):
+    z = load_golden(name)
+    args = (bf16_bits_to_f32(z["q_bits"]), bf16_bits_to_f32(z["kv_bits"]), z["q_weight"], z["k_weight"],
+            int(z["heads"]), float(z["eps"]))
+    check_close(cross.cross_diff_attention(*args), z["out_ref"], max_abs=1e-5, mean_abs=1e-6)
+    a, b = cross.cross_branches(*args)
+    check_close(dense.merge_heads(a), z["branch_a"], max_abs=1e-5, mean_abs=1e-6)
+    check_close(dense.merge_heads(b), z["branch_b"], max_abs=1e-5, mean_abs=1e-6)
+    lam = z["lam"]
+    ref = z["branch_a"] - np.repeat(lam, 128)[None, None, :] * z["branch_b"]
+    check_close(cross.cross_diff_attention(*args, lam=lam), ref, max_abs=1e-5, mean_abs=1e-6)
+
+
+def test_cross_oracle_hoisted_keys_and_invariants():
+    """Pre-normed keys with k_weight=None give the same result; lambda = 0 is branch A; identical branches
+    cancel exactly."""
+    z = load_golden("cross_h4_q200_kv128")
+    q2, kv = bf16_bits_to_f32(z["q_bits"]), bf16_bits_to_f32(z["kv_bits"]).astype(np.float64)
+    args = (z["q_weight"], z["k_weight"], 4, 1e-6)
+    full = cross.cross_diff_attention(q2, kv, *args)
+    k, kd, v = np.split(kv, 3, axis=-1)
+    normed = [dense.merge_heads(dense.rms_norm(t.reshape(2, 128, 4, 64).transpose(0, 2, 1, 3), z["k_weight"], 1e-6))
+              for t in (k, kd)]
+    hoisted = np.concatenate([*normed, v], -1)
+    check_close(cross.cross_diff_attention(q2, hoisted, z["q_weight"], None, 4), full, max_abs=1e-6, mean_abs=1e-7)
+    check_close(cross.cross_diff_attention(q2, kv, *args, lam=np.zeros(2, np.float32)), z["branch_a"],
+                max_abs=1e-5, mean_abs=1e-6)
+    qs, kvs = np.split(q2, 2, axis=-1), np.split(kv, 3, axis=-1)
+    same = cross.cross_diff_attention(np.concatenate([qs[0], qs[0]], -1), np.concatenate([kvs[0], kvs[0], kvs[2]], -1),
+                                      *args)
+    assert np.abs(same).max() == 0.0
 
 
 @pytest.mark.parametrize("name", BAND)
