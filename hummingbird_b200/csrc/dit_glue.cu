@@ -11,6 +11,8 @@
 //
 // Rounding follows the torch ops they replace: every step computes in fp32 and rounds to bf16 where the
 // unfused sequence stores a bf16 tensor (h after each residual, 1 + scale, 1 - gate and its sigmoid, silu).
+#include <algorithm>
+
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -46,23 +48,27 @@ struct ResNormParams {
 };
 
 constexpr int kRowWarps = 8;
+constexpr size_t kResNormMaxSmem = 96 * 1024;  // per-column vectors of every batch element: nb * 5 * d fp32
 
-// One warp per row; lane l holds the 16-byte chunks l, l + 32, ... (NC chunks, d = 256 NC).
+// Persistent row stream: the per-column vectors of every batch element (sigmoid(1 - gate), the RMSNorm weight,
+// 1 + scale, shift, local; fp32 with the torch sequence's roundings) are evaluated once per block into shared
+// memory; then warp w of W walks rows w, w + W, ..., loading the next row's h and y while it finishes the
+// current one. Lane l holds the 16-byte chunks l, l + 32, ... of a row (NC chunks, d = 256 NC).
+constexpr int kStreamBlocksPerSm = 2;
+
+__host__ __device__ constexpr int colv_floats(int nb, int d) { return nb * 5 * d; }
+
 template <int NC>
-__global__ void __launch_bounds__(32 * kRowWarps) residual_norm_kernel(const ResNormParams p) {
-  const int r = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (r >= p.rows) return;
-  const int b = r / p.rows_per_batch, t = r - b * p.rows_per_batch;
+__device__ __forceinline__ void residual_norm_row(const ResNormParams& p, const float* cv, int r, const uint4 (&hv4)[NC],
+                                                  const uint4 (&yv4)[NC], int lane) {
+  constexpr int d = 256 * NC;
+  const float* gm = cv;           // sigmoid(1 - gate)
+  const float* wv = cv + d;       // RMSNorm weight
+  const float* sc1 = cv + 2 * d;  // 1 + scale
+  const float* shv = cv + 3 * d;  // shift
+  const float* lv = cv + 4 * d;   // local
+  const int t = r % p.rows_per_batch;
   uint16_t* hr = p.h + (size_t)r * p.ldh;
-  uint4 hv4[NC], yv4[NC];
-#pragma unroll
-  for (int i = 0; i < NC; ++i) hv4[i] = ld_v4(hr + (i * 32 + lane) * 8);
-  if (p.y) {
-    const uint16_t* yr = p.y + (size_t)r * p.ldy;
-#pragma unroll
-    for (int i = 0; i < NC; ++i) yv4[i] = ld_v4(yr + (i * 32 + lane) * 8);
-  }
   const bool add_local = p.local && t >= p.local_row0;
   float v[NC][8];
   float ss = 0.f;
@@ -74,24 +80,16 @@ __global__ void __launch_bounds__(32 * kRowWarps) residual_norm_kernel(const Res
       float yv[8];
       unpack8(yv4[i], yv);
       if (p.gate) {
-        float g[8];
-        unpack8(ld_v4(p.gate + (size_t)b * p.ldc + c), g);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const float a = round_bf16(1.f - g[e]);
-          const float gm = round_bf16(1.f / (1.f + __expf(-a)));
-          v[i][e] = round_bf16(v[i][e] + yv[e] * gm);
-        }
+        for (int e = 0; e < 8; ++e) v[i][e] = round_bf16(v[i][e] + yv[e] * gm[c + e]);
       } else {
 #pragma unroll
         for (int e = 0; e < 8; ++e) v[i][e] = round_bf16(v[i][e] + yv[e]);
       }
     }
     if (add_local) {
-      float lv[8];
-      unpack8(ld_v4(p.local + c), lv);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) v[i][e] = round_bf16(v[i][e] + lv[e]);
+      for (int e = 0; e < 8; ++e) v[i][e] = round_bf16(v[i][e] + lv[c + e]);
     }
     if (p.y || add_local) *reinterpret_cast<uint4*>(hr + c) = pack8(v[i]);
 #pragma unroll
@@ -100,32 +98,138 @@ __global__ void __launch_bounds__(32 * kRowWarps) residual_norm_kernel(const Res
   if (!p.x) return;
 #pragma unroll
   for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-  const float inv = rsqrtf(ss / static_cast<float>(p.d) + p.eps);
+  const float inv = rsqrtf(ss / static_cast<float>(d) + p.eps);
   uint16_t* xr = p.x + (size_t)r * p.ldx;
 #pragma unroll
   for (int i = 0; i < NC; ++i) {
     const int c = (i * 32 + lane) * 8;
-    float w[8], o[8];
-    unpack8(ld_v4(p.w + c), w);
+    float o[8];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) o[e] = round_bf16(__fmul_rn(v[i][e], inv) * w[e]);
+    for (int e = 0; e < 8; ++e) o[e] = round_bf16(__fmul_rn(v[i][e], inv) * wv[c + e]);
     if (p.scale) {
-      float sc[8], sh[8];
-      unpack8(ld_v4(p.scale + (size_t)b * p.ldc + c), sc);
-      unpack8(ld_v4(p.shift + (size_t)b * p.ldc + c), sh);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) o[e] = sh[e] + o[e] * round_bf16(1.f + sc[e]);
+      for (int e = 0; e < 8; ++e) o[e] = shv[c + e] + o[e] * sc1[c + e];
     }
     *reinterpret_cast<uint4*>(xr + c) = pack8(o);
   }
 }
 
 template <int NC>
-void launch_residual_norm(const ResNormParams& p, cudaStream_t s) {
-  residual_norm_kernel<NC><<<(p.rows + kRowWarps - 1) / kRowWarps, 32 * kRowWarps, 0, s>>>(p);
+__device__ __forceinline__ void residual_norm_load(const ResNormParams& p, int r, int lane, uint4 (&hv4)[NC],
+                                                   uint4 (&yv4)[NC]) {
+  const uint16_t* hr = p.h + (size_t)r * p.ldh;
+#pragma unroll
+  for (int i = 0; i < NC; ++i) hv4[i] = ld_v4(hr + (i * 32 + lane) * 8);
+  if (p.y) {
+    const uint16_t* yr = p.y + (size_t)r * p.ldy;
+#pragma unroll
+    for (int i = 0; i < NC; ++i) yv4[i] = ld_v4(yr + (i * 32 + lane) * 8);
+  }
+}
+
+template <int NC>
+__global__ void __launch_bounds__(32 * kRowWarps, kStreamBlocksPerSm)
+    residual_norm_kernel(const ResNormParams p, int nb) {
+  constexpr int d = 256 * NC;
+  extern __shared__ float colv[];
+  const int lane = threadIdx.x & 31;
+  const int total_warps = gridDim.x * kRowWarps;
+  int r = blockIdx.x * kRowWarps + (threadIdx.x >> 5);
+  uint4 hv4[NC], yv4[NC];
+  if (r < p.rows) residual_norm_load<NC>(p, r, lane, hv4, yv4);  // in flight during the column setup
+  for (int idx = threadIdx.x; idx < nb * (d / 8); idx += 32 * kRowWarps) {
+    const int b = idx / (d / 8), c = (idx - b * (d / 8)) * 8;
+    float* cv = colv + colv_floats(b, d);
+    float u[8];
+    if (p.y && p.gate) {
+      unpack8(ld_v4(p.gate + (size_t)b * p.ldc + c), u);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float a = round_bf16(1.f - u[e]);
+        cv[c + e] = round_bf16(1.f / (1.f + __expf(-a)));
+      }
+    }
+    if (p.x) {
+      unpack8(ld_v4(p.w + c), u);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) cv[d + c + e] = u[e];
+    }
+    if (p.scale) {
+      unpack8(ld_v4(p.scale + (size_t)b * p.ldc + c), u);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) cv[2 * d + c + e] = round_bf16(1.f + u[e]);
+      unpack8(ld_v4(p.shift + (size_t)b * p.ldc + c), u);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) cv[3 * d + c + e] = u[e];
+    }
+    if (p.local) {
+      unpack8(ld_v4(p.local + c), u);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) cv[4 * d + c + e] = u[e];
+    }
+  }
+  __syncthreads();
+  while (r < p.rows) {  // warp-uniform
+    const int rn = r + total_warps;
+    uint4 hn[NC], yn[NC];
+    if (rn < p.rows) residual_norm_load<NC>(p, rn, lane, hn, yn);
+    residual_norm_row<NC>(p, colv + colv_floats(r / p.rows_per_batch, d), r, hv4, yv4, lane);
+#pragma unroll
+    for (int i = 0; i < NC; ++i) {
+      hv4[i] = hn[i];
+      yv4[i] = yn[i];
+    }
+    r = rn;
+  }
+}
+
+// One launch per group of batch elements whose column vectors fit kResNormMaxSmem.
+template <int NC>
+int launch_residual_norm(const ResNormParams& p, cudaStream_t s) {
+  const int nb_all = (p.rows + p.rows_per_batch - 1) / p.rows_per_batch;
+  const int per_launch = static_cast<int>(kResNormMaxSmem / (colv_floats(1, 256 * NC) * sizeof(float)));
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) != cudaSuccess) return HB_ERR_LAUNCH;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  static bool configured[64] = {};
+  if (dev < 64 && !configured[dev]) {
+    if (cudaFuncSetAttribute(residual_norm_kernel<NC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kResNormMaxSmem) != cudaSuccess)
+      return HB_ERR_LAUNCH;
+    configured[dev] = true;
+  }
+  for (int b0 = 0; b0 < nb_all; b0 += per_launch) {
+    const int nb = nb_all - b0 < per_launch ? nb_all - b0 : per_launch;
+    const long long row0 = (long long)b0 * p.rows_per_batch;
+    ResNormParams q = p;
+    q.rows = static_cast<int>(std::min<long long>(p.rows - row0, (long long)nb * p.rows_per_batch));
+    q.h = p.h + row0 * p.ldh;
+    if (p.y) q.y = p.y + row0 * p.ldy;
+    if (p.x) q.x = p.x + row0 * p.ldx;
+    if (p.gate) q.gate = p.gate + (size_t)b0 * p.ldc;
+    if (p.scale) q.scale = p.scale + (size_t)b0 * p.ldc;
+    if (p.shift) q.shift = p.shift + (size_t)b0 * p.ldc;
+    const size_t smem = colv_floats(nb, 256 * NC) * sizeof(float);
+    const int need = (q.rows + kRowWarps - 1) / kRowWarps;
+    const int grid = need < sms * kStreamBlocksPerSm ? need : sms * kStreamBlocksPerSm;
+    residual_norm_kernel<NC><<<grid, 32 * kRowWarps, smem, s>>>(q, nb);
+    if (cudaGetLastError() != cudaSuccess) return HB_ERR_LAUNCH;
+  }
+  return HB_OK;
 }
 
 // ------------------------------------------------------------------ GLU (+ per-row int8 quantisation)
+// rintf(x / s) with x / s the correctly rounded fp32 quotient, from q0 = x * fl(1 / s): q0 is within
+// 2^-23 |x / s| of x / s, so unless q0 lies within max(|q0|, 1) * 2^-19 of a half-integer, x / s and its rounded
+// value sit strictly between the same two half-integers as q0 and round to the same integer; the rare
+// remaining cases take the IEEE division.
+__device__ __forceinline__ float rint_quotient(float x, float s, float rs) {
+  const float q0 = x * rs;
+  const float n = rintf(q0);
+  if (fabsf(fabsf(q0 - n) - 0.5f) <= fmaxf(fabsf(q0), 1.f) * 0x1p-19f) return rintf(__fdiv_rn(x, s));
+  return n;
+}
+
 constexpr int kGluThreads = 256;
 constexpr int kGluChunks = 4;  // F <= 256 * 8 * 4 = 8192
 
@@ -158,7 +262,7 @@ __global__ void __launch_bounds__(kGluThreads) glu_rows_kernel(const uint16_t* _
     unpack8(ga[i], b);
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
-      const float silu = round_bf16(b[e] / (1.f + __expf(-b[e])));
+      const float silu = round_bf16(__fdividef(b[e], 1.f + __expf(-b[e])));
       zv[i][e] = round_bf16(a[e] * silu);
       amax = fmaxf(amax, fabsf(zv[i][e]));
     }
@@ -173,6 +277,7 @@ __global__ void __launch_bounds__(kGluThreads) glu_rows_kernel(const uint16_t* _
 #pragma unroll
     for (int w = 1; w < kGluThreads / 32; ++w) amax = fmaxf(amax, warp_max[w]);
     const float s = amax == 0.f ? 1.f : __fdiv_rn(amax, 127.f);
+    const float rs = __frcp_rn(s);
     if (tid == 0) scale[r] = s;
 #pragma unroll
     for (int i = 0; i < kGluChunks; ++i) {
@@ -181,7 +286,7 @@ __global__ void __launch_bounds__(kGluThreads) glu_rows_kernel(const uint16_t* _
       uint32_t packed[2] = {0u, 0u};
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
-        const float qv = fminf(fmaxf(rintf(__fdiv_rn(zv[i][e], s)), -127.f), 127.f);
+        const float qv = fminf(fmaxf(rint_quotient(zv[i][e], s, rs), -127.f), 127.f);
         packed[e >> 2] |= (static_cast<uint32_t>(static_cast<int>(qv)) & 0xFFu) << (8 * (e & 3));
       }
       *reinterpret_cast<uint2*>(q + (size_t)r * ldq + k) = make_uint2(packed[0], packed[1]);
@@ -244,16 +349,15 @@ extern "C" int hb_dit_residual_norm(void* h, int64_t ldh, const void* y, int64_t
                   static_cast<const uint16_t*>(weight), static_cast<uint16_t*>(x), ldx, rows, rows_per_batch, d,
                   eps};
   switch (d / 256) {
-    case 1: launch_residual_norm<1>(p, stream); break;
-    case 2: launch_residual_norm<2>(p, stream); break;
-    case 3: launch_residual_norm<3>(p, stream); break;
-    case 4: launch_residual_norm<4>(p, stream); break;
-    case 5: launch_residual_norm<5>(p, stream); break;
-    case 6: launch_residual_norm<6>(p, stream); break;
-    case 7: launch_residual_norm<7>(p, stream); break;
-    default: launch_residual_norm<8>(p, stream); break;
+    case 1: return launch_residual_norm<1>(p, stream);
+    case 2: return launch_residual_norm<2>(p, stream);
+    case 3: return launch_residual_norm<3>(p, stream);
+    case 4: return launch_residual_norm<4>(p, stream);
+    case 5: return launch_residual_norm<5>(p, stream);
+    case 6: return launch_residual_norm<6>(p, stream);
+    case 7: return launch_residual_norm<7>(p, stream);
+    default: return launch_residual_norm<8>(p, stream);
   }
-  return cudaGetLastError() == cudaSuccess ? HB_OK : HB_ERR_LAUNCH;
 }
 
 extern "C" int hb_glu_rows(const void* glu, int64_t ldg, int rows, int F, void* z, int64_t ldz, void* q, int64_t ldq,

@@ -55,6 +55,24 @@ def test_residual_norm_matches_torch_ops(cuda_lib, d):
     _close_bf16(h, torch.addcmul(h0, y, torch.sigmoid(1 - gate[:, None, :])))
 
 
+def test_residual_norm_many_batch_elements(cuda_lib):
+    """More batch elements than one launch holds column vectors for (d = 2048: two per launch), ragged rows."""
+    from hummingbird_b200 import dit_glue as glue
+    g = torch.Generator(device="cuda").manual_seed(15)
+    bsz, t, d, eps = 5, 37, 2048, 1e-6
+    h0 = _bf(bsz, t, d, gen=g, scale=2.0)
+    y = _bf(bsz, t, d, gen=g)
+    cond = _bf(bsz, 3 * d, gen=g, scale=0.5)
+    gate, scale, shift = cond[:, :d], cond[:, d:2 * d], cond[:, 2 * d:]
+    w = (1 + 0.02 * torch.randn(d, generator=g, device="cuda")).to(torch.bfloat16)
+    h = h0.clone()
+    x = glue.residual_norm(h, y=y, gate=gate, weight=w, scale=scale, shift=shift, eps=eps)
+    h_ref = torch.addcmul(h0, y, torch.sigmoid(1 - gate[:, None, :]))
+    x_ref = torch.addcmul(shift[:, None, :], F.rms_norm(h_ref, (d,), w, eps), 1 + scale[:, None, :])
+    _close_bf16(h, h_ref)
+    _close_bf16(x, x_ref)
+
+
 def test_glu_matches_torch_and_quantises_with_the_quantiser_rules(cuda_lib):
     from hummingbird_b200 import dit_glue as glue
     from hummingbird_b200.w8a8 import quantize_rows
