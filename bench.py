@@ -252,7 +252,7 @@ def _flush_l2(flush) -> None:
 
 
 def _event_median(fn, steps: int, warmup: int, flush) -> float:
-    """Median CUDA-event time of `fn` on the current stream, L2 flushed before each call. A ~50 us GPU sleep
+    """Median CUDA-event time of `fn` on the current stream, L2 flushed before each call. A ~0.5 ms GPU sleep
     between the flush and the start event keeps the GPU busy while the host enqueues the call, so the
     interval holds the device work of `fn` and not the host's launch latency."""
     import torch
@@ -263,7 +263,7 @@ def _event_median(fn, steps: int, warmup: int, flush) -> float:
     stream = torch.cuda.current_stream()
     for _ in range(steps):
         _flush_l2(flush)
-        torch.cuda._sleep(100_000)
+        torch.cuda._sleep(1_000_000)
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record(stream)
         fn()
@@ -380,7 +380,7 @@ def time_w8a8(device, steps: int, warmup: int) -> dict:
     torch.cuda.synchronize()
     for i in range(steps):
         _flush_l2(flush)
-        torch.cuda._sleep(200_000)  # the GPU waits ~0.1 ms while the host enqueues the four launches
+        torch.cuda._sleep(1_000_000)  # the GPU waits ~0.5 ms while the host enqueues the four launches
         one(ev[i])
     torch.cuda.synchronize()
     med = lambda j, k: statistics.median(e[j].elapsed_time(e[k]) for e in ev)  # noqa: E731
@@ -469,7 +469,8 @@ def time_dit_clip(device, ff_quant: str, world: int = 1, clips: int = 3) -> dict
             "config": "120 s clip: B=2 (CFG), 2,584 latents + 64 memory, 24 blocks, d 1024, 16 heads, 8 pingpong "
                       "steps, 128 context tokens, random weights",
             "mlp": "W8A8" if ff_quant == "w8a8" else "bf16 cuBLAS", "finite": finite,
-            "glue": "fused row kernels (residual + RMSNorm + adaLN, GLU + quantise, head RMSNorm)",
+            "glue": "fused row kernels (residual + RMSNorm + adaLN, GLU + quantise) and the fused "
+                    "differential cross-attention kernel",
             "parallelism": f"one clip over {world} GPUs: token rows x{world}, self-attention head pairs x{world}, "
                            "2 NCCL all-to-alls per block" if world > 1 else "single GPU",
             "how": "one denoise step captured in a CUDA graph, replayed 8 times per clip; CUDA events, max over ranks"}
@@ -598,16 +599,18 @@ def time_band_song_layer(device, world: int, rank: int, steps: int = 20, warmup:
 
 
 # ----------------------------------------------------------------------------------------------- CPU baseline
-def cpu_band_baseline(qkv_dev, w, q_rows: int) -> dict:
-    """The oracle port on the host cores over queries [0, q_rows) of the rank-0 workload."""
+def cpu_band_baseline(qkv_dev, w, q_rows: int, min_seconds: float = 10.0) -> dict:
+    """The oracle port on the host cores over queries [0, q_rows) of the rank-0 workload, repeated until at
+    least `min_seconds` of wall time have been measured."""
     sys.path.insert(0, str(ROOT))
     from oracle.cpu_baseline import time_band_sample
+    q_rows = min(q_rows, qkv_dev.shape[1])
     rows = min(qkv_dev.shape[1], q_rows + WINDOW)
     qkv = qkv_dev[:, :rows].float().cpu().numpy()
-    r = time_band_sample(qkv, w.q_norm, w.k_norm, w.inv_freq, HEADS, WINDOW, w.lam, q_rows)
+    r = time_band_sample(qkv, w.q_norm, w.k_norm, w.inv_freq, HEADS, WINDOW, w.lam, q_rows, min_seconds=min_seconds)
     return {"value": r["flops"] / r["seconds"] / 1e12, "unit": "TFLOP/s", "cores": r["cores"], "kind": "port",
-            "sample": f"queries 0..{q_rows} of config 2 (8 heads, window 128), fp32 numpy oracle, "
-                      f"{r['cores']}-process spawn pool, {r['seconds']:.2f} s"}
+            "sample": f"queries 0..{q_rows} of config 2 (8 heads, window 128) x {r['passes']} passes, fp32 numpy "
+                      f"oracle, {r['cores']}-process spawn pool, {r['seconds']:.1f} s"}
 
 
 def run_reference(args, result_out):
@@ -620,7 +623,7 @@ def run_reference(args, result_out):
     from hummingbird_b200.workloads import band_inputs
     from oracle.cpu_baseline import shutdown, time_band_sample
     w = band_inputs("cpu", seed=1, length=L_PER_GPU, d_model=512, heads=HEADS, window=WINDOW)
-    q_rows = 8192
+    q_rows = L_PER_GPU  # each step: the whole config-2 call
     qkv = w.qkv[:, :q_rows + WINDOW].float().numpy()
     for _ in range(args.warmup):
         time_band_sample(qkv, w.q_norm, w.k_norm, w.inv_freq, HEADS, WINDOW, w.lam, q_rows)
@@ -635,8 +638,8 @@ def run_reference(args, result_out):
     line = {"metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": secs / args.steps * 1e3, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
-            "config": {"workload": "band diff-attn, config 2 sample: queries 0..8192 of L=82,688, 8 heads, "
-                                   "window 128 (bf16 inputs, fp32 compute)"},
+            "config": {"workload": "band diff-attn, config 2: all 82,688 query rows, 8 heads, window 128 "
+                                   "(bf16 inputs, fp32 compute)"},
             "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": cores, "kind": "port",
                              "sample": f"{q_rows} queries per step; JAX absent, fp32 numpy restatement of the "
                                        "reference XLA path (oracle/band.py)"},
@@ -663,7 +666,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="hb", choices=["hb", "reference"])
     ap.add_argument("--no-secondary", action="store_true", help="skip the dense / W8A8 lines (N = 1)")
-    ap.add_argument("--cpu-rows", type=int, default=32768, help="queries in the CPU-baseline sample")
+    ap.add_argument("--cpu-rows", type=int, default=L_PER_GPU, help="queries in the CPU-baseline sample")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     if args.impl == "reference":

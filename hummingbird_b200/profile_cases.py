@@ -1,0 +1,67 @@
+"""Fixed-shape calls of one hot-path kernel each, for profilers (`ncu -k <kernel> -s <skip> -c <count>`).
+
+    python -m hummingbird_b200.profile_cases band    # config 2: SAME-L band attention, B=1, L=82,688, 8 heads
+    python -m hummingbird_b200.profile_cases dense   # dense DiT self-attention, B=2, L=2,648, 16 heads
+    python -m hummingbird_b200.profile_cases cross   # DiT cross-attention, B=2, 2,648 queries, 128 context, 16 heads
+
+Each case builds its seeded synthetic inputs (`hummingbird_b200.workloads`), makes `--calls` calls (default 3)
+on the current GPU and prints a checksum of the last output. Nothing is timed here: the bench times.
+"""
+from __future__ import annotations
+
+import argparse
+
+import torch
+
+
+def band(calls: int) -> torch.Tensor:
+    from hummingbird_b200.band_attention import band_attention, pack_norm
+    from hummingbird_b200.workloads import band_inputs
+    w = band_inputs("cuda")
+    lam, freqs = torch.from_numpy(w.lam).cuda(), torch.from_numpy(w.inv_freq).cuda()
+    qn, kn = pack_norm(w.q_norm, "cuda"), pack_norm(w.k_norm, "cuda")
+    for _ in range(calls):
+        out = band_attention(w.qkv, qn, kn, freqs, w.heads, 64, w.window, lam=lam)
+    return out
+
+
+def dense(calls: int) -> torch.Tensor:
+    from hummingbird_b200 import dense_attention as hb
+    from hummingbird_b200.workloads import dense_inputs
+    w = dense_inputs("cuda", batch=2, length=2648)
+    f = lambda a: torch.from_numpy(a).cuda()  # noqa: E731
+    cos, sin, mask = hb.tables(2648, f(w.inv_freq), f(w.valid))
+    for _ in range(calls):
+        out = hb.dense_attention(w.qkv, f(w.q_weight), f(w.k_weight), cos, sin, mask, w.heads, 64, w.half, w.eps,
+                                 lam=f(w.lam))
+    return out
+
+
+def cross(calls: int) -> torch.Tensor:
+    from hummingbird_b200.cross_attention import cross_attention, cross_kv
+    g = torch.Generator(device="cuda").manual_seed(7)
+    batch, length, heads, context = 2, 2648, 16, 128
+    q2 = torch.randn(batch, length, 2 * heads * 64, generator=g, device="cuda").to(torch.bfloat16)
+    kv = cross_kv(torch.randn(batch, context, 3 * heads * 64, generator=g, device="cuda").to(torch.bfloat16),
+                  1 + 0.02 * torch.randn(64, generator=g, device="cuda"), heads, 1e-6)
+    qw = 1 + 0.02 * torch.randn(64, generator=g, device="cuda")
+    for _ in range(calls):
+        out = cross_attention(q2, kv, qw, None, heads)
+    return out
+
+
+CASES = {"band": band, "dense": dense, "cross": cross}
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("case", choices=sorted(CASES))
+    ap.add_argument("--calls", type=int, default=3)
+    args = ap.parse_args()
+    out = CASES[args.case](args.calls)
+    torch.cuda.synchronize()
+    print(args.case, "ok", float(out.float().abs().mean()))
+
+
+if __name__ == "__main__":
+    main()

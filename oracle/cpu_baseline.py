@@ -85,10 +85,12 @@ def _band_task(args):
 
 
 def time_band_sample(qkv: np.ndarray, q_norm: dict, k_norm: dict, freqs: np.ndarray, heads: int, window: int,
-                     lam: np.ndarray, q_rows: int, workers: int | None = None, chunk: int = 256) -> dict:
+                     lam: np.ndarray, q_rows: int, workers: int | None = None, chunk: int = 256,
+                     min_seconds: float = 0.0) -> dict:
     """Time the oracle on queries [0, q_rows) of `qkv` (float32 `(1, L, 5 H 64)`, placed in shared memory),
-    split into `chunk`-row tasks (each reading its +-window halo) over a spawn pool. Returns seconds, FLOPs
-    and the worker count."""
+    split into `chunk`-row tasks (each reading its +-window halo) over a spawn pool, repeating the whole sample
+    until `min_seconds` have passed (at least once). Returns seconds, FLOPs of all passes, the pass count and
+    the worker count."""
     from multiprocessing import shared_memory
     length = qkv.shape[1]
     p = pool(workers)
@@ -102,12 +104,18 @@ def time_band_sample(qkv: np.ndarray, q_norm: dict, k_norm: dict, freqs: np.ndar
             tasks.append((shm.name, qkv.shape, q_norm, k_norm, freqs, heads, window, lam, lo, hi, q0, q1))
         p.map(_band_task, tasks[: min(len(tasks), _WORKERS)])  # warm the workers (imports, BLAS, mapping)
         t0 = time.perf_counter()
-        p.map(_band_task, tasks)
+        passes = 0
+        while True:
+            p.map(_band_task, tasks)
+            passes += 1
+            if time.perf_counter() - t0 >= min_seconds:
+                break
         seconds = time.perf_counter() - t0
     finally:
         shm.close()
         shm.unlink()
-    return {"seconds": seconds, "flops": band_flops(length, heads, window, 0, q_rows), "cores": _WORKERS}
+    return {"seconds": seconds, "flops": passes * band_flops(length, heads, window, 0, q_rows), "passes": passes,
+            "cores": _WORKERS}
 
 
 def _dense_task(args):
