@@ -20,7 +20,7 @@ CSRC = PKG / "csrc"
 LIB = PKG / "libhb_b200.so"
 COMM_LIB = PKG / "libhb_comm.so"
 COMM_SOURCES = ["comm.cu"]
-SOURCES = ["abi.cu", "attn_kernel.cu", "dense_attn.cu", "band_attn.cu", "band_fused.cu", "cross_attn.cu", "w8a8.cu",
+SOURCES = ["abi.cu", "attn_kernel.cu", "attn_dense.cu", "dense_attn.cu", "band_attn.cu", "band_fused.cu", "cross_attn.cu", "w8a8.cu",
            "dit_glue.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

@@ -38,4 +38,7 @@ struct AttnParams {
 // Launch the shared differential-attention kernel on `stream`. Returns a cudaError_t as int.
 int launch_diff_attention(const AttnParams& p, cudaStream_t stream);
 
+// Dense mode only (window < 0, q_begin = 0): scores and probabilities in separate TMEM buffers (attn_dense.cu).
+int launch_dense_attention(const AttnParams& p, cudaStream_t stream);
+
 }  // namespace hb

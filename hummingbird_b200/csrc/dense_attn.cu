@@ -7,7 +7,7 @@
 //                         caller's cos / signed-sin lane tables -> bf16   (dense_attention.py:61-69)
 //   v:                    bf16(v * mask)                                   (dense_attention.py:77)
 // The 1/sqrt(64) score scale is applied in the softmax (exact: a power of two).
-// Main kernel: attn_kernel.cu (dense mode: every key, no key mask, dense_attention.py:79-83).
+// Main kernel: attn_dense.cu (every key, no key mask, dense_attention.py:79-83).
 #include <atomic>
 
 #include <cuda_runtime.h>
@@ -181,7 +181,7 @@ extern "C" int hb_dense_diff_attn(const void* qkv, int64_t qkv_row_stride, const
   ap.lam_pair0 = pair_begin;
   ap.out = static_cast<uint16_t*>(out);
   ap.out_row_stride = out_row_stride;
-  return launch_diff_attention(ap, stream) == cudaSuccess ? HB_OK : HB_ERR_LAUNCH;
+  return launch_dense_attention(ap, stream) == cudaSuccess ? HB_OK : HB_ERR_LAUNCH;
 }
 
 // ------------------------------------------------------------------------------------------------------
