@@ -23,6 +23,26 @@ namespace {
 constexpr int kPrepThreads = 256;
 constexpr int kUnitsPerGroup = 4;  // units (one row x one section x one head) per 8-thread group, loads issued together
 
+// n / d for 0 <= n < 2^31 by a multiply-high and a shift (the round-up reciprocal method: multiplier
+// ceil(2^p / d) with p = 31 + ceil(log2 d)); replaces the integer divisions of the unit decode.
+struct FastDiv {
+  uint32_t d, mul, shift;
+  void init(uint32_t div) {
+    d = div;
+    if (div == 1) {
+      mul = 0;
+      shift = 0;
+      return;
+    }
+    uint32_t l = 0;
+    while ((1ull << l) < div) ++l;
+    const uint32_t pw = 31 + l;
+    mul = static_cast<uint32_t>(((1ull << pw) + div - 1) / div);
+    shift = pw - 32;
+  }
+  __device__ __forceinline__ uint32_t operator()(uint32_t n) const { return d == 1 ? n : (__umulhi(n, mul) >> shift); }
+};
+
 struct DensePrepParams {
   const uint16_t* qkv;
   int64_t qkv_row_stride;
@@ -39,11 +59,43 @@ struct DensePrepParams {
   uint8_t* ws;
   int ntiles;
   int units;  // B * ntiles * 128 * 5 * heads (< 2^31, checked on the host)
+  FastDiv by_heads, by_sections, by_rows;
 };
+
+struct UnitPos {
+  int hl, s, row, b;
+};
+
+__device__ __forceinline__ UnitPos decode_unit(const DensePrepParams& p, uint32_t u) {
+  UnitPos x;
+  const uint32_t rs = p.by_heads(u);
+  x.hl = static_cast<int>(u - rs * static_cast<uint32_t>(p.heads));
+  const uint32_t br = p.by_sections(rs);
+  x.s = static_cast<int>(rs - br * kSections);
+  const uint32_t bb = p.by_rows(br);
+  x.row = static_cast<int>(br - bb * static_cast<uint32_t>(p.ntiles * kTileRows));
+  x.b = static_cast<int>(bb);
+  return x;
+}
+
+// 8 consecutive fp32 values; 16-byte vector loads when kVec (the caller checked the alignment)
+template <bool kVec>
+__device__ __forceinline__ void load8f(const float* src, float (&v)[8]) {
+  if constexpr (kVec) {
+    const float4 a = __ldg(reinterpret_cast<const float4*>(src));
+    const float4 c = __ldg(reinterpret_cast<const float4*>(src) + 1);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = c.x; v[5] = c.y; v[6] = c.z; v[7] = c.w;
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = __ldg(src + i);
+  }
+}
 
 // Unit u = ((b * rows_pad + row) * 5 + section) * heads + head: consecutive 8-thread groups take consecutive
 // units (consecutive 128-byte pieces of a qkv row), and each group takes kUnitsPerGroup units spaced a grid
 // apart, loading all of them before computing.
+template <bool kVec>
 __global__ void __launch_bounds__(kPrepThreads) dense_prep_kernel(const DensePrepParams p) {
   const int lane = threadIdx.x & 31;
   const int c = threadIdx.x & 7;
@@ -51,53 +103,48 @@ __global__ void __launch_bounds__(kPrepThreads) dense_prep_kernel(const DensePre
   const int hc8 = p.half >> 3;
   const int group = blockIdx.x * (kPrepThreads / 8) + (threadIdx.x >> 3);
   const int stride = gridDim.x * (kPrepThreads / 8);
-  const int rows_pad = p.ntiles * kTileRows;
   uint4 raw[kUnitsPerGroup];
 #pragma unroll
   for (int k = 0; k < kUnitsPerGroup; ++k) {
     const int u = group + k * stride;
     raw[k] = make_uint4(0, 0, 0, 0);
     if (u < p.units) {
-      const int hl = u % p.heads;
-      const int rs = u / p.heads;
-      const int s = rs % kSections;
-      const int br = rs / kSections;
-      const int row = br % rows_pad, b = br / rows_pad;
-      if (row < p.L)
-        raw[k] = ld_nc_v4(p.qkv + ((size_t)b * p.L + row) * p.qkv_row_stride + (size_t)s * p.H_total * kHeadDim +
-                          (size_t)(p.head0 + hl) * kHeadDim + c * 8);
+      const UnitPos x = decode_unit(p, static_cast<uint32_t>(u));
+      if (x.row < p.L)
+        raw[k] = ld_nc_v4(p.qkv + ((size_t)x.b * p.L + x.row) * p.qkv_row_stride + (size_t)x.s * p.H_total * kHeadDim +
+                          (size_t)(p.head0 + x.hl) * kHeadDim + c * 8);
     }
   }
 #pragma unroll
   for (int k = 0; k < kUnitsPerGroup; ++k) {
     const int u = group + k * stride;
     if (u >= p.units) break;  // uniform within the 8-thread group (same u)
-    const int hl = u % p.heads;
-    const int rs = u / p.heads;
-    const int s = rs % kSections;
-    const int br = rs / kSections;
-    const int row = br % rows_pad, b = br / rows_pad;
-    const bool valid = row < p.L;
-    float x[8];
-    unpack8(raw[k], x);
+    const UnitPos x = decode_unit(p, static_cast<uint32_t>(u));
+    const bool valid = x.row < p.L;
+    float xv[8];
+    unpack8(raw[k], xv);
     uint4 outv;
-    if (s == 2) {
-      const float m = valid ? __uint_as_float((uint32_t)p.vmask[b * p.mask_bstride + row * p.mask_lstride] << 16) : 0.f;
+    if (x.s == 2) {
+      const float m = valid ? __uint_as_float((uint32_t)p.vmask[x.b * p.mask_bstride + x.row * p.mask_lstride] << 16)
+                            : 0.f;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) x[i] *= m;
-      outv = pack8(x);
+      for (int i = 0; i < 8; ++i) xv[i] *= m;
+      outv = pack8(xv);
     } else {
       float ss = 0.f;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) ss = fmaf(x[i], x[i], ss);
+      for (int i = 0; i < 8; ++i) ss = fmaf(xv[i], xv[i], ss);
       ss += __shfl_xor_sync(gmask, ss, 1);
       ss += __shfl_xor_sync(gmask, ss, 2);
       ss += __shfl_xor_sync(gmask, ss, 4);
       const float inv = rsqrtf(ss * (1.f / kHeadDim) + p.eps);
-      const float* w = (s == 0 || s == 3) ? p.q_w : p.k_w;
-      float y[8];
+      float wv[8], y[8];
+      load8f<kVec>(((x.s == 0 || x.s == 3) ? p.q_w : p.k_w) + c * 8, wv);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) y[i] = x[i] * inv * __ldg(w + c * 8 + i);
+      for (int i = 0; i < 8; i += 2) {  // (x * inv) * w, each product rounded (packed pairs)
+        fmul2(y[i], y[i + 1], xv[i], xv[i + 1], inv, inv);
+        fmul2(y[i], y[i + 1], y[i], y[i + 1], wv[i], wv[i + 1]);
+      }
       const uint4 yb = pack8(y);  // RMSNorm output rounded to bf16 (dense_attention.py:66)
       const int src = (lane & 24) | rope_partner_chunk(c, hc8);
       uint4 pb;
@@ -109,18 +156,23 @@ __global__ void __launch_bounds__(kPrepThreads) dense_prep_kernel(const DensePre
       unpack8(yb, yv);
       unpack8(pb, pv);
       if (valid) {
-        const float* cr = p.cos + (size_t)row * p.table_stride + c * 8;
-        const float* sr = p.sin + (size_t)row * p.table_stride + c * 8;
+        float cr[8], sr[8];
+        load8f<kVec>(p.cos + (size_t)x.row * p.table_stride + c * 8, cr);
+        load8f<kVec>(p.sin + (size_t)x.row * p.table_stride + c * 8, sr);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) y[i] = yv[i] * __ldg(cr + i) + pv[i] * __ldg(sr + i);
+        for (int i = 0; i < 8; i += 2) {  // y cos + partner * signed sin
+          float t0, t1;
+          fmul2(t0, t1, pv[i], pv[i + 1], sr[i], sr[i + 1]);
+          ffma2(y[i], y[i + 1], yv[i], yv[i + 1], cr[i], cr[i + 1], t0, t1);
+        }
       } else {
 #pragma unroll
         for (int i = 0; i < 8; ++i) y[i] = 0.f;
       }
       outv = pack8(y);
     }
-    uint8_t* dst = p.ws + prep_tile_offset(b, hl, s, row / kTileRows, p.heads, p.ntiles) +
-                   sw128_offset(row % kTileRows, c);
+    uint8_t* dst = p.ws + prep_tile_offset(x.b, x.hl, x.s, x.row / kTileRows, p.heads, p.ntiles) +
+                   sw128_offset(x.row % kTileRows, c);
     *reinterpret_cast<uint4*>(dst) = outv;
   }
 }
@@ -162,10 +214,19 @@ extern "C" int hb_dense_diff_attn(const void* qkv, int64_t qkv_row_stride, const
   if (units >= (int64_t(1) << 31)) return HB_ERR_SHAPE;
   DensePrepParams pp{static_cast<const uint16_t*>(qkv), qkv_row_stride, batch, length, num_heads, 2 * pair_begin,
                      heads, q_weight, k_weight, cos, sin, table_stride, static_cast<const uint16_t*>(vmask),
-                     mask_batch_stride, mask_row_stride, eps, half, static_cast<uint8_t*>(workspace), ntiles, (int)units};
+                     mask_batch_stride, mask_row_stride, eps, half, static_cast<uint8_t*>(workspace), ntiles, (int)units,
+                     {}, {}, {}};
+  pp.by_heads.init(static_cast<uint32_t>(heads));
+  pp.by_sections.init(kSections);
+  pp.by_rows.init(static_cast<uint32_t>(ntiles * kTileRows));
   const int64_t groups = (units + kUnitsPerGroup - 1) / kUnitsPerGroup;
   const int pblocks = (int)((groups + kPrepThreads / 8 - 1) / (kPrepThreads / 8));
-  dense_prep_kernel<<<pblocks, kPrepThreads, 0, stream>>>(pp);
+  // 16-byte loads of the weights and lane tables when their rows are 16-byte aligned
+  const bool vec = aligned16(q_weight) && aligned16(k_weight) && aligned16(cos) && aligned16(sin) && table_stride % 4 == 0;
+  if (vec)
+    dense_prep_kernel<true><<<pblocks, kPrepThreads, 0, stream>>>(pp);
+  else
+    dense_prep_kernel<false><<<pblocks, kPrepThreads, 0, stream>>>(pp);
   if (cudaGetLastError() != cudaSuccess) return HB_ERR_LAUNCH;
 
   AttnParams ap{};

@@ -54,6 +54,22 @@ def test_dense_identical_branches_cancel(cuda_lib):
     assert np.abs(_run(z)).max() == 0.0
 
 
+def test_dense_tables_without_16_byte_alignment(cuda_lib):
+    """Lane tables whose rows are not 16-byte aligned take the prologue's scalar-load path: same bits."""
+    from hummingbird_b200 import dense_attention as hb
+    z = load_golden("dense_h4_l200_full")
+    qkv = bf16_cuda(z["qkv_bits"])
+    cos, sin, mask = hb.tables(200, f32_cuda(z["inv_freq"]), f32_cuda(z["valid"]))
+    args = (f32_cuda(z["q_weight"]), f32_cuda(z["k_weight"]))
+    ref = hb.dense_attention(qkv, *args, cos, sin, mask, 4, 64, 32, float(z["eps"]))
+    pad_c = torch.zeros(200, 129, device="cuda")
+    pad_s = torch.zeros(200, 129, device="cuda")
+    pad_c[:, 1:], pad_s[:, 1:] = cos, sin
+    out = hb.dense_attention(qkv, *args, pad_c[:, 1:], pad_s[:, 1:], mask, 4, 64, 32, float(z["eps"]))
+    torch.cuda.synchronize()
+    assert torch.equal(out.view(torch.int16), ref.view(torch.int16))
+
+
 def test_dense_pair_sharding_matches_full(cuda_lib):
     z = load_golden("dense_h4_l200_full")
     full = _run(z, lam=z["lam"])
