@@ -1,4 +1,6 @@
-// Shared tcgen05 differential-attention kernel (dense DiT self-attention and SAME-L band attention).
+// tcgen05 differential-attention kernel over prepared tiles, used for SAME-L band attention with windows
+// wider than the fused band kernel handles (window > 128). It accepts the dense mode too (window < 0); the
+// dense path runs attn_dense.cu.
 //
 // One CTA computes one 128-query tile of one head for BOTH differential branches:
 //   A = softmax(Q  K^T  / 8) V,   B = softmax(Qd Kd^T / 8) V,   out = A - lambda * B   (fp32, one bf16 cast)
