@@ -2,7 +2,7 @@
 
 JAX is not installable here, so `tests/golden/_jaxshim/jax` (a numpy stand-in for the few JAX calls on
 the reference's XLA path) is put on `sys.path` and the reference package `sa3jax` is imported from the
-reference checkout (default `/root/reference`, or `$HB_REFERENCE`). The reference then runs in fp32
+reference checkout (`$HB_REFERENCE`, else the checkout's path in the build container). The reference then runs in fp32
 (`dtypes.FP32_PARITY`) through its own functions:
 
 * dense: `sa3jax.dit._self_attention` (dit.py:185-200) with `DiTConfig(attention="xla", differential=True)`,

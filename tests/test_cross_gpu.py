@@ -1,6 +1,6 @@
 """GPU parity: the sm_100a differential cross-attention (through the C ABI) against golden vectors made by the
 reference's own `_cross_attention` and against the fp32 oracle. Tolerance: max-abs 2e-2, mean-abs 2e-3 (the
-attention tolerance of the north star), plus the bf16 rounding of outputs larger than 1."""
+attention tolerance), plus the bf16 rounding of outputs larger than 1."""
 import numpy as np
 import pytest
 import torch

@@ -1,5 +1,5 @@
 """GPU parity: the sm_100a dense differential attention (through the C ABI) against the reference's golden
-vectors and the fp32 oracle. Tolerance: max-abs 2e-2, mean-abs 2e-3 (north star), plus the bf16 rounding
+vectors and the fp32 oracle. Tolerance: max-abs 2e-2, mean-abs 2e-3 (the attention tolerance), plus the bf16 rounding
 of outputs larger than 1."""
 import numpy as np
 import pytest
