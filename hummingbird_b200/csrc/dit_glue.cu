@@ -26,6 +26,14 @@ namespace {
 
 __device__ __forceinline__ float round_bf16(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
+// Two bf16 roundings with one packed conversion (the conversions share the transcendental pipe with exp and
+// the reciprocal, which bounds the GLU); the same round-to-nearest-even as round_bf16 on each value.
+__device__ __forceinline__ void round_bf16_pair(float& a, float& b) {
+  const uint32_t w = pack_bf16x2(a, b);
+  a = bf16_lo(w);
+  b = bf16_hi(w);
+}
+
 __device__ __forceinline__ uint4 ld_v4(const uint16_t* p) { return __ldg(reinterpret_cast<const uint4*>(p)); }
 
 // ------------------------------------------------------------------ residual + RMSNorm + modulation
@@ -81,15 +89,19 @@ __device__ __forceinline__ void residual_norm_row(const ResNormParams& p, const 
       unpack8(yv4[i], yv);
       if (p.gate) {
 #pragma unroll
-        for (int e = 0; e < 8; ++e) v[i][e] = round_bf16(v[i][e] + yv[e] * gm[c + e]);
+        for (int e = 0; e < 8; ++e) v[i][e] = v[i][e] + yv[e] * gm[c + e];
       } else {
 #pragma unroll
-        for (int e = 0; e < 8; ++e) v[i][e] = round_bf16(v[i][e] + yv[e]);
+        for (int e = 0; e < 8; ++e) v[i][e] = v[i][e] + yv[e];
       }
+#pragma unroll
+      for (int e = 0; e < 8; e += 2) round_bf16_pair(v[i][e], v[i][e + 1]);
     }
     if (add_local) {
 #pragma unroll
-      for (int e = 0; e < 8; ++e) v[i][e] = round_bf16(v[i][e] + lv[c + e]);
+      for (int e = 0; e < 8; ++e) v[i][e] = v[i][e] + lv[c + e];
+#pragma unroll
+      for (int e = 0; e < 8; e += 2) round_bf16_pair(v[i][e], v[i][e + 1]);
     }
     if (p.y || add_local) *reinterpret_cast<uint4*>(hr + c) = pack8(v[i]);
 #pragma unroll
@@ -105,7 +117,9 @@ __device__ __forceinline__ void residual_norm_row(const ResNormParams& p, const 
     const int c = (i * 32 + lane) * 8;
     float o[8];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) o[e] = round_bf16(__fmul_rn(v[i][e], inv) * wv[c + e]);
+    for (int e = 0; e < 8; ++e) o[e] = __fmul_rn(v[i][e], inv) * wv[c + e];
+#pragma unroll
+    for (int e = 0; e < 8; e += 2) round_bf16_pair(o[e], o[e + 1]);
     if (p.scale) {
 #pragma unroll
       for (int e = 0; e < 8; ++e) o[e] = shv[c + e] + o[e] * sc1[c + e];
@@ -219,16 +233,28 @@ int launch_residual_norm(const ResNormParams& p, cudaStream_t s) {
 }
 
 // ------------------------------------------------------------------ GLU (+ per-row int8 quantisation)
-// rintf(x / s) with x / s the correctly rounded fp32 quotient, from q0 = x * fl(1 / s): q0 is within
-// 2^-23 |x / s| of x / s, so unless q0 lies within max(|q0|, 1) * 2^-19 of a half-integer, x / s and its rounded
-// value sit strictly between the same two half-integers as q0 and round to the same integer; the rare
-// remaining cases take the IEEE division.
+// rintf(x / s) with x / s the correctly rounded fp32 quotient (the quantiser's rule), from q0 = x * fl(1 / s).
+// q0 is within 2^-23 |x / s| of the exact quotient and fl(x / s) within 2^-24 |x / s|, so for |q0| < 128.5 the
+// two differ by less than 2^-15: unless q0 lies within 2^-14 of a half-integer, fl(x / s) rounds to the same
+// integer n as q0. Quotients of magnitude 128.5 and above clamp to +-127 either way. Near-ties and a q0 that is
+// not finite (a reciprocal that overflowed) take the IEEE division.
+// n is rounded by adding and subtracting kRoundMagic = 1.5 * 2^23: for |v| < 2^22 the sum lies in [2^23, 2^24),
+// where the fp32 spacing is 1, so fl(v + kRoundMagic) - kRoundMagic is v rounded to the nearest integer, ties
+// to even (kRoundMagic is even), as rintf gives; larger |v| keep their sign and a magnitude far above 127.
+// These are adds on the FMA pipe in place of rounding and conversion instructions on the transcendental pipe,
+// which the exponentials and reciprocals of the GLU already saturate.
+constexpr float kRoundMagic = 12582912.f;
+constexpr float kNearHalf = 0.5f - 0x1p-14f;
 __device__ __forceinline__ float rint_quotient(float x, float s, float rs) {
   const float q0 = x * rs;
-  const float n = rintf(q0);
-  if (fabsf(fabsf(q0 - n) - 0.5f) <= fmaxf(fabsf(q0), 1.f) * 0x1p-19f) return rintf(__fdiv_rn(x, s));
+  const float n = __fsub_rn(__fadd_rn(q0, kRoundMagic), kRoundMagic);
+  if (!(fabsf(q0 - n) < kNearHalf)) return rintf(__fdiv_rn(x, s));
   return n;
 }
+
+// The low byte (two's complement) of an integer-valued v in [-127, 127]: v + kRoundMagic is exact and its bit
+// pattern is that of kRoundMagic (low byte 0) plus v.
+__device__ __forceinline__ uint32_t int8_bits(float v) { return __float_as_uint(__fadd_rn(v, kRoundMagic)) & 0xFFu; }
 
 constexpr int kGluThreads = 256;
 constexpr int kGluChunks = 4;  // F <= 256 * 8 * 4 = 8192
@@ -261,10 +287,13 @@ __global__ void __launch_bounds__(kGluThreads) glu_rows_kernel(const uint16_t* _
     unpack8(va[i], a);
     unpack8(ga[i], b);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const float silu = round_bf16(__fdividef(b[e], 1.f + __expf(-b[e])));
-      zv[i][e] = round_bf16(a[e] * silu);
-      amax = fmaxf(amax, fabsf(zv[i][e]));
+    for (int e = 0; e < 8; e += 2) {
+      float s0 = __fdividef(b[e], 1.f + __expf(-b[e])), s1 = __fdividef(b[e + 1], 1.f + __expf(-b[e + 1]));
+      round_bf16_pair(s0, s1);  // silu, stored as bf16 by the unfused sequence
+      zv[i][e] = a[e] * s0;
+      zv[i][e + 1] = a[e + 1] * s1;
+      round_bf16_pair(zv[i][e], zv[i][e + 1]);
+      amax = fmaxf(amax, fmaxf(fabsf(zv[i][e]), fabsf(zv[i][e + 1])));
     }
     if constexpr (!kQuant) *reinterpret_cast<uint4*>(z + (size_t)r * ldz + k) = pack8(zv[i]);
   }
@@ -287,7 +316,7 @@ __global__ void __launch_bounds__(kGluThreads) glu_rows_kernel(const uint16_t* _
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
         const float qv = fminf(fmaxf(rint_quotient(zv[i][e], s, rs), -127.f), 127.f);
-        packed[e >> 2] |= (static_cast<uint32_t>(static_cast<int>(qv)) & 0xFFu) << (8 * (e & 3));
+        packed[e >> 2] |= int8_bits(qv) << (8 * (e & 3));
       }
       *reinterpret_cast<uint2*>(q + (size_t)r * ldq + k) = make_uint2(packed[0], packed[1]);
     }

@@ -3,6 +3,7 @@
     python -m hummingbird_b200.profile_cases band    # config 2: SAME-L band attention, B=1, L=82,688, 8 heads
     python -m hummingbird_b200.profile_cases dense   # dense DiT self-attention, B=2, L=2,648, 16 heads
     python -m hummingbird_b200.profile_cases cross   # DiT cross-attention, B=2, 2,648 queries, 128 context, 16 heads
+    python -m hummingbird_b200.profile_cases glue    # DiT row kernels: residual + RMSNorm + adaLN, GLU + int8
 
 Each case builds its seeded synthetic inputs (`hummingbird_b200.workloads`), makes `--calls` calls (default 3)
 on the current GPU and prints a checksum of the last output. Nothing is timed here: the bench times.
@@ -50,7 +51,24 @@ def cross(calls: int) -> torch.Tensor:
     return out
 
 
-CASES = {"band": band, "dense": dense, "cross": cross}
+def glue(calls: int) -> torch.Tensor:
+    """One DiT block's row kernels at the 120 s clip's shapes: the residual add + RMSNorm + adaLN before the
+    next block (`residual_norm_kernel`, B=2, 2,648 rows, d 1,024) and the GLU + int8 quantiser feeding the MLP's
+    second GEMM (`glu_rows_kernel`, 5,296 rows, 2 x 4,096 columns in)."""
+    from hummingbird_b200 import dit_glue
+    g = torch.Generator(device="cuda").manual_seed(11)
+    batch, length, d, f = 2, 2648, 1024, 4096
+    bf = lambda *s: torch.randn(*s, generator=g, device="cuda").to(torch.bfloat16)  # noqa: E731
+    h, y, cond, weight, proj = bf(batch, length, d), bf(batch, length, d), bf(batch, 6 * d), bf(d), bf(
+        batch * length, 2 * f)
+    for _ in range(calls):
+        x = dit_glue.residual_norm(h, y=y, gate=cond[:, 5 * d:], weight=weight, scale=cond[:, :d],
+                                   shift=cond[:, d:2 * d], eps=1e-6)
+        q, _ = dit_glue.glu(proj, quantize=True)
+    return x.float().mean() + q.float().mean()
+
+
+CASES = {"band": band, "dense": dense, "cross": cross, "glue": glue}
 
 
 def main() -> None:
