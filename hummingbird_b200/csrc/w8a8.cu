@@ -14,6 +14,7 @@
 #include "../../include/hb_b200.h"
 #include "abi_common.h"
 #include "hb_sm100.cuh"
+#include "quant_common.cuh"
 
 namespace hb {
 
@@ -45,14 +46,13 @@ namespace {
 constexpr int kQuantThreads = 128;
 constexpr int kQuantChunks = 4;  // rows up to 4096 elements held in registers
 
-__device__ __forceinline__ uint2 quantize8(const uint4& v, float s) {
+__device__ __forceinline__ uint2 quantize8(const uint4& v, float s, float rs) {
   const uint32_t w[4] = {v.x, v.y, v.z, v.w};
   uint32_t packed[2] = {0, 0};
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     const float xv = (i & 1) ? bf16_hi(w[i >> 1]) : bf16_lo(w[i >> 1]);
-    const float qv = fminf(fmaxf(rintf(__fdiv_rn(xv, s)), -127.f), 127.f);
-    packed[i >> 2] |= (static_cast<uint32_t>(static_cast<int>(qv)) & 0xFFu) << (8 * (i & 3));
+    packed[i >> 2] |= int8_bits(quantize_int8(xv, s, rs)) << (8 * (i & 3));
   }
   return make_uint2(packed[0], packed[1]);
 }
@@ -93,16 +93,17 @@ __global__ void __launch_bounds__(kQuantThreads) quant_rows_kernel(const uint16_
   __syncthreads();
   amax = fmaxf(fmaxf(warp_max[0], warp_max[1]), fmaxf(warp_max[2], warp_max[3]));
   const float s = amax == 0.f ? 1.f : __fdiv_rn(amax, 127.f);
+  const float rs = __frcp_rn(s);
   if (tid == 0) scale[r] = s;
   if (resident) {
 #pragma unroll
     for (int i = 0; i < kQuantChunks; ++i) {
       const int k = (tid + kQuantThreads * i) * 8;
-      if (k < K) *reinterpret_cast<uint2*>(qr + k) = quantize8(v[i], s);
+      if (k < K) *reinterpret_cast<uint2*>(qr + k) = quantize8(v[i], s, rs);
     }
   } else {
     for (int k = tid * 8; k < K; k += kQuantThreads * 8)
-      *reinterpret_cast<uint2*>(qr + k) = quantize8(__ldg(reinterpret_cast<const uint4*>(xr + k)), s);
+      *reinterpret_cast<uint2*>(qr + k) = quantize8(__ldg(reinterpret_cast<const uint4*>(xr + k)), s, rs);
   }
 }
 
