@@ -20,8 +20,11 @@ CSRC = PKG / "csrc"
 LIB = PKG / "libhb_b200.so"
 COMM_LIB = PKG / "libhb_comm.so"
 COMM_SOURCES = ["comm.cu"]
-SOURCES = ["abi.cu", "attn_kernel.cu", "attn_dense.cu", "dense_attn.cu", "band_attn.cu", "band_fused.cu", "cross_attn.cu", "w8a8.cu",
+SOURCES = ["abi.cu", "attn_kernel.cu", "attn_dense.cu", "dense_attn.cu", "band_attn.cu", "cross_attn.cu", "w8a8.cu",
            "dit_glue.cu"]
+# Compiled as whole-program device code (no -rdc) into an object linked into the same library: ptxas ignores
+# setmaxnreg in relocatable device code, and these kernels rebalance registers between warpgroups with it.
+WHOLE_PROGRAM_SOURCES = ["band_fused.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
@@ -34,20 +37,35 @@ def nvcc() -> str:
 
 def build(verbose: bool = False, force: bool = False) -> Path:
     srcs = [CSRC / s for s in SOURCES]
-    deps = srcs + list(CSRC.glob("*.h")) + list(CSRC.glob("*.cuh")) + [ROOT / "include" / "hb_b200.h"]
+    wp_srcs = [CSRC / s for s in WHOLE_PROGRAM_SOURCES]
+    deps = srcs + wp_srcs + list(CSRC.glob("*.h")) + list(CSRC.glob("*.cuh")) + [ROOT / "include" / "hb_b200.h"]
     if LIB.exists() and not force and all(LIB.stat().st_mtime >= d.stat().st_mtime for d in deps):
         return LIB
+    common = [*ARCH, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr", "-I",
+              str(ROOT / "include")]
+    if verbose:
+        common.insert(0, "-Xptxas=-v")
+
+    def run(cmd):
+        if verbose:
+            print(" ".join(cmd), flush=True)
+        res = subprocess.run(cmd, capture_output=True, text=True)
+        if res.returncode != 0:
+            raise RuntimeError(f"nvcc failed ({res.returncode}):\n{res.stdout}\n{res.stderr}")
+        if verbose:
+            print(res.stdout, res.stderr, sep="\n")
+
+    objs = []
+    for src in wp_srcs:
+        obj = LIB.parent / (src.stem + ".wp.o")
+        run([nvcc(), *common, "-c", "-o", str(obj), str(src)])
+        objs.append(obj)
     tmp = LIB.with_suffix(".so.tmp")
-    cmd = [nvcc(), *ARCH, "-O3", "-lineinfo", "-std=c++17", "-rdc=true", "-shared", "-Xcompiler", "-fPIC",
-           "--expt-relaxed-constexpr", "-I", str(ROOT / "include"), "-o", str(tmp), *map(str, srcs)]
-    if verbose:
-        cmd.insert(1, "-Xptxas=-v")
-        print(" ".join(cmd), flush=True)
-    res = subprocess.run(cmd, capture_output=True, text=True)
-    if res.returncode != 0:
-        raise RuntimeError(f"nvcc failed ({res.returncode}):\n{res.stdout}\n{res.stderr}")
-    if verbose:
-        print(res.stdout, res.stderr, sep="\n")
+    try:
+        run([nvcc(), *common, "-rdc=true", "-shared", "-o", str(tmp), *map(str, srcs), *map(str, objs)])
+    finally:
+        for obj in objs:
+            obj.unlink(missing_ok=True)
     os.replace(tmp, LIB)
     return LIB
 

@@ -6,20 +6,30 @@
 // kt-1, kt, kt+1, so it is prepared once and kept in a 3-slot ring (window <= 128 means a query tile needs
 // at most the key tiles qt-1, qt, qt+1).
 //
-// Roles (16 warps):
-//   warp 0       3-D TMA (128B swizzle, rows past the sequence read as zero) of the raw q, q_diff tile of
-//                each unit into a double buffer and of each new k, k_diff, v tile into the ring slot
-//   warp 1       TMEM allocation (512 columns) and the single MMA-issuing thread
-//   warps 4-7    softmax of branch A (one query row per thread); writes 1/l_A per row for the epilogue
-//   warps 8-11   softmax of branch B, then the per-tile epilogue: out = O_A / l_A - lambda O_B / l_B, bf16
-//   warps 2-3, 12-15  preparation, in place in shared memory (DyT and RoPE only mix dims of one row):
-//                DyT gamma * tanh(alpha x) + beta and RoPE in fp32 with angles fp32(pos) * inv_freq
-//                reduced to [-pi, pi] (Cody-Waite) for the hardware sin/cos, then bf16 (q, k rounded once)
-// TMEM: S_A [0,128) (P_A in [0,64)), S_B [128,256), O_A/O_B double-buffered by tile parity at
-// [256,320)/[320,384) and [384,448)/[448,512), so the epilogue of tile j overlaps tile j+1.
+// Roles (16 warps, four warpgroups; registers rebalanced with setmaxnreg):
+//   WG0  warp 0      3-D TMA (128B swizzle, rows past the sequence read as zero) of the raw q, q_diff tile of
+//                    each unit into a double buffer and of each new k, k_diff, v tile into a ring slot
+//        warp 1      TMEM allocation (512 columns) and the single MMA-issuing thread
+//        warps 2-3   preparation (below)
+//   WG1  warps 4-7   softmax of branch A, WG2 warps 8-11 softmax of branch B: one query row per thread
+//   WG3  warps 12-15 preparation, and the epilogue of each unit: out = O_A / l_A - lambda O_B / l_B, bf16
+//   Preparation, in place in shared memory (DyT and RoPE only mix dims of one row): DyT gamma * tanh(alpha x)
+//   + beta and RoPE in fp32 with angles fp32(pos) * inv_freq reduced to [-pi, pi] (Cody-Waite) for the
+//   hardware sin/cos, then bf16 (q, k rounded once).
+// TMEM: per branch a score buffer S (128 columns), a probability buffer P (64 columns of packed bf16) and an
+// accumulator O (64 columns): S_A [0,128), S_B [128,256), P_A [256,320), P_B [320,384), O_A [384,448),
+// O_B [448,512). The softmax loads a tile's scores with one wait and releases S at once, so S of the next key
+// tile (of this unit or the next) is computed while it works; P is written once the previous P V has read
+// it. O is single-buffered: the epilogue warps load it and release it before the next unit's first P V.
 //
-// MMA order per key tile i of unit j: S_A(i), PV_B(i-1), S_B(i), PV_A(i), with PV_B(last) of unit j
-// issued after S_A(0) of unit j+1. A key tile is released to the producers right after its last PV_B.
+// MMA order over the CTA's flat list of key tiles t: S_A(0), S_B(0); then for each t: S_A(t+1), S_B(t+1),
+// PV_A(t), PV_B(t). A key tile's ring slot is released after the last P V that reads it.
+//
+// This file is compiled without relocatable device code (whole-program; see build.py): with -rdc ptxas
+// ignores setmaxnreg. Its kernel records errors in its own status word (band_fused_take_status).
+#define HB_WHOLE_PROGRAM 1
+// One in eight key pairs' exponentials on the FMA pipe (measured best for this kernel; the others use 1 in 4).
+#define HB_POLY_MASK 7
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
@@ -31,32 +41,15 @@
 
 namespace hb {
 
-#ifdef HB_TRACE
-// Debug builds only (-DHB_TRACE): %clock timestamps of pipeline events, one slot per traced thread, kept in
-// shared memory while the kernel runs (no global traffic) and copied out by CTA 0 at the end.
-__device__ unsigned int g_trace[8][2048];
-__device__ unsigned int g_trace_n[8];
-constexpr int kTraceSlots = 5, kTraceEvents = 240;
-constexpr int kTraceBytes = kTraceSlots * kTraceEvents * 8 + 64;
-#define TRACE(slot, id, t0)                                                         \
-  do {                                                                              \
-    trace_slot = (slot);                                                            \
-    if (trace_n < kTraceEvents) {                                                   \
-      trace_buf[((slot) * kTraceEvents + trace_n) * 2] = (id);                      \
-      trace_buf[((slot) * kTraceEvents + trace_n) * 2 + 1] = (unsigned)clock();     \
-      ++trace_n;                                                                    \
-    }                                                                               \
-  } while (0)
-#else
-constexpr int kTraceBytes = 0;
-#define TRACE(slot, id, t0) \
-  do {                      \
-  } while (0)
-#endif
-
 namespace {
 
 constexpr int kThreads = 512;
+// Launched with 128 registers per thread (512 threads, one CTA per SM); the softmax warpgroups take 168,
+// the other two give up to 88: 2 * 168 + 2 * 88 = 4 * 128, the registers the block was launched with.
+constexpr int kRegsSoftmax = 168;
+constexpr int kRegsOther = 88;
+static_assert(2 * kRegsSoftmax + 2 * kRegsOther == 4 * 128, "register split must equal the launch allocation");
+constexpr int kLaunchRegs = 128;
 constexpr int kPrepWarps = 6;  // warps 2, 3 and 12-15
 constexpr int kPrepThreads = 32 * kPrepWarps;
 constexpr int kSlots = 3;
@@ -64,19 +57,28 @@ constexpr int kSlotBytes = 3 * kTileBytes;  // K, Kd, V
 constexpr int kQBytes = 2 * kTileBytes;     // Q, Qd
 constexpr int kOffQ = kSlots * kSlotBytes;
 constexpr int kOffBars = kOffQ + 2 * kQBytes;
-constexpr int kNumBars = 26;
+constexpr int kNumBars = 28;
 constexpr int kOffMisc = kOffBars + kNumBars * 8;
 constexpr int kOffNorm = kOffMisc + 16;
 constexpr int kNormStride = 132;
-constexpr int kOffScaleA = kOffNorm + 2 * kNormStride * 4;
-constexpr int kOffFreq = kOffScaleA + 2 * kTileRows * 4;
-constexpr int kOffTrace = kOffFreq + 32 * 4;
-constexpr int kSmemBytes = kOffTrace + kTraceBytes + 1024;
+constexpr int kOffScale = kOffNorm + 2 * kNormStride * 4;  // [2 units][2 branches][128 rows]
+constexpr int kOffFreq = kOffScale + 2 * 2 * kTileRows * 4;
+constexpr int kSmemBytes = kOffFreq + 32 * 4 + 1024;
+constexpr uint32_t kColS = 0, kColP = 256, kColO = 384;
 // 2 pi = kTwoPi1 + kTwoPi2 + kTwoPi3 (fp32 parts of 2 pi taken to 60 digits) and fp32(1 / (2 pi))
 constexpr float kTwoPi1 = 6.2831854820251465f, kTwoPi2 = -1.7484555314695172e-07f, kTwoPi3 = -6.8604980400235275e-15f;
 constexpr float kInvTwoPi = 0.15915493667125702f;
 constexpr float kScoreScale = 1.4426950408889634f * 0.125f;
 constexpr float kRescaleThreshold = 8.0f;
+
+template <uint32_t N>
+__device__ __forceinline__ void regs_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void regs_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
 
 struct Unit {
   int b, h, qt, klo, khi;
@@ -124,6 +126,12 @@ __device__ __forceinline__ uint32_t band_bits(int kc, int q, int window, int row
   return upto & (0xffffffffu << lo);
 }
 
+// Whether the 32-key chunk starting at kc holds an in-band key for any of the warp's query rows
+// [qw_lo, qw_lo + 31] (warp-uniform).
+__device__ __forceinline__ bool chunk_live(int kc, int qw_lo, int window, int rows) {
+  return kc < rows && kc <= qw_lo + 31 + window && kc + 31 >= qw_lo - window;
+}
+
 __device__ __forceinline__ bool same_run(const Unit& a, const Unit& b) { return a.b == b.b && a.h == b.h; }
 
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
@@ -131,10 +139,36 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
   return __all_sync(0xffffffffu, ok);
 }
 
+#ifndef HB_SLACK_SLEEP_NS
+#define HB_SLACK_SLEEP_NS 200
+#endif
+#ifndef HB_MMA_SLEEP_NS
+#define HB_MMA_SLEEP_NS 0
+#endif
+#ifndef HB_SOFT_SLEEP_NS
+#define HB_SOFT_SLEEP_NS 100
+#endif
+// Waits on the critical path (MMA issuer, softmax): a tight poll unless a sleep is configured.
+__device__ __forceinline__ bool mma_wait(uint64_t* bar, uint32_t parity) {
+  return HB_MMA_SLEEP_NS ? mbar_wait_sleep(bar, parity, HB_MMA_SLEEP_NS) : mbar_wait(bar, parity);
+}
+__device__ __forceinline__ bool soft_wait(uint64_t* bar, uint32_t parity) {
+  return HB_SOFT_SLEEP_NS ? mbar_wait_sleep(bar, parity, HB_SOFT_SLEEP_NS) : mbar_wait(bar, parity);
+}
+// Waits of the roles with slack (TMA producer, preparation, epilogue).
+__device__ __forceinline__ bool slack_wait(uint64_t* bar, uint32_t parity) {
+  return HB_SLACK_SLEEP_NS ? mbar_wait_sleep(bar, parity, HB_SLACK_SLEEP_NS) : mbar_wait(bar, parity);
+}
+__device__ __forceinline__ bool warp_slack_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+  const bool ok = slack_wait(bar, parity) && !*abort_flag;
+  return __all_sync(0xffffffffu, ok);
+}
+
 // cos / sin of an fp32 angle: Cody-Waite reduction by 2 pi (three-part constant, FMA) to |r| <= ~pi, then
 // the hardware approximations on the reduced argument (absolute error ~2^-21 there).
 __device__ __forceinline__ void sincos_reduced(float x, float& sn, float& cs) {
-  const float k = rintf(x * kInvTwoPi);
+  // k = rint(x / 2 pi) by adding and subtracting 1.5 * 2^23 (exact for |x / 2 pi| < 2^22), on the FMA pipe
+  const float k = __fadd_rn(__fmaf_rn(x, kInvTwoPi, 12582912.0f), -12582912.0f);
   float r = fmaf(-k, kTwoPi1, x);
   r = fmaf(-k, kTwoPi2, r);
   r = fmaf(-k, kTwoPi3, r);
@@ -142,10 +176,23 @@ __device__ __forceinline__ void sincos_reduced(float x, float& sn, float& cs) {
   cs = __cosf(r);
 }
 
+// Eight consecutive fp32 values of shared memory, read at the point of use (kept out of registers across
+// the row loop: the preparation warps run with a small register budget).
+__device__ __forceinline__ void lds8(const float* src, float (&v)[8]) {
+  const uint32_t a = smem_u32(src);
+  asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3]) : "r"(a));
+  asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(v[4]), "=f"(v[5]), "=f"(v[6]), "=f"(v[7]) : "r"(a + 16));
+}
+
+#ifndef HB_BAND_PACK
+#define HB_BAND_PACK pack_bf16x2
+#endif
+
 // Transform one 128-row tile of two raw sections (q/q_diff or k/k_diff, landed by TMA in the SW128 image)
 // in place: DyT, RoPE, bf16. Four threads own a row; each owns two 8-dim chunks: for rotary dims a chunk
 // and its rotate-half partner (so RoPE needs no exchange and each angle is evaluated once), the remaining
-// chunks in pairs.
+// chunks in pairs. norm = {alpha, gamma[64], beta[64]} with gamma and beta 16-byte aligned in shared memory
+// (alpha at index 3). The arithmetic runs on packed fp32 pairs: alpha x, gamma t + beta and the rotation.
 __device__ __forceinline__ void prep_inplace(const BandFusedParams& p, int tile, const float* norm,
                                              const float* freqs, uint8_t* buf0, uint8_t* buf1, int pt, int nthreads) {
   const int sub = pt & 3, rg = pt >> 2, ngroups = nthreads >> 2;
@@ -153,15 +200,7 @@ __device__ __forceinline__ void prep_inplace(const BandFusedParams& p, int tile,
   const bool rot = sub < hc8;
   const int c0 = rot ? sub : 2 * hc8 + 2 * (sub - hc8);
   const int c1 = rot ? sub + hc8 : c0 + 1;
-  const float alpha = norm[0];
-  float g0[8], b0[8], g1[8], b1[8];
-#pragma unroll
-  for (int e = 0; e < 8; ++e) {
-    g0[e] = norm[1 + c0 * 8 + e];
-    b0[e] = norm[65 + c0 * 8 + e];
-    g1[e] = norm[1 + c1 * 8 + e];
-    b1[e] = norm[65 + c1 * 8 + e];
-  }
+  const float alpha = norm[3];
 #pragma unroll 1
   for (int r = rg; r < kTileRows; r += ngroups) {
     const int row = tile * kTileRows + r;
@@ -172,29 +211,55 @@ __device__ __forceinline__ void prep_inplace(const BandFusedParams& p, int tile,
 #pragma unroll
       for (int e = 0; e < 8; ++e) sincos_reduced(pos * freqs[8 * sub + e], sn[e], cs[e]);  // fp32(pos) * inv_freq
     }
-#pragma unroll
+#pragma unroll 1
     for (int sec = 0; sec < 2; ++sec) {
       uint8_t* buf = sec ? buf1 : buf0;
       uint4* p0 = reinterpret_cast<uint4*>(buf + sw128_offset(r, c0));
       uint4* p1 = reinterpret_cast<uint4*>(buf + sw128_offset(r, c1));
-      float x0[8], x1[8], y0[8], y1[8];
-      unpack8(*p0, x0);
-      unpack8(*p1, x1);
+      float y0[8], y1[8], g[8], bt[8];
+      unpack8(*p0, y0);
+      unpack8(*p1, y1);
+      lds8(norm + 4 + c0 * 8, g);  // gamma / beta read at the point of use: the prep warps' register budget is small
+      lds8(norm + 68 + c0 * 8, bt);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        y0[e] = fmaf(g0[e], tanh_approx(alpha * x0[e]), b0[e]);
-        y1[e] = fmaf(g1[e], tanh_approx(alpha * x1[e]), b1[e]);
+      for (int e = 0; e < 8; e += 2) {
+        fmul2(y0[e], y0[e + 1], y0[e], y0[e + 1], alpha, alpha);
+        y0[e] = tanh_approx(y0[e]);
+        y0[e + 1] = tanh_approx(y0[e + 1]);
+        ffma2(y0[e], y0[e + 1], g[e], g[e + 1], y0[e], y0[e + 1], bt[e], bt[e + 1]);
+      }
+      lds8(norm + 4 + c1 * 8, g);
+      lds8(norm + 68 + c1 * 8, bt);
+#pragma unroll
+      for (int e = 0; e < 8; e += 2) {
+        fmul2(y1[e], y1[e + 1], y1[e], y1[e + 1], alpha, alpha);
+        y1[e] = tanh_approx(y1[e]);
+        y1[e + 1] = tanh_approx(y1[e + 1]);
+        ffma2(y1[e], y1[e + 1], g[e], g[e + 1], y1[e], y1[e + 1], bt[e], bt[e + 1]);
       }
       if (rot) {  // d < half pairs with d + half: y_d cos - y_{d+half} sin, y_{d+half} cos + y_d sin
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const float a = y0[e], b = y1[e];
-          y0[e] = a * cs[e] - b * sn[e];
-          y1[e] = b * cs[e] + a * sn[e];
+        for (int e = 0; e < 8; e += 2) {
+          float u0, u1, v0, v1;
+          fmul2(u0, u1, y0[e], y0[e + 1], cs[e], cs[e + 1]);
+          fmul2(v0, v1, y1[e], y1[e + 1], cs[e], cs[e + 1]);
+          ffma2(u0, u1, y1[e], y1[e + 1], -sn[e], -sn[e + 1], u0, u1);
+          ffma2(v0, v1, y0[e], y0[e + 1], sn[e], sn[e + 1], v0, v1);
+          y0[e] = u0;
+          y0[e + 1] = u1;
+          y1[e] = v0;
+          y1[e + 1] = v1;
         }
       }
-      *p0 = valid ? pack8(y0) : make_uint4(0, 0, 0, 0);
-      *p1 = valid ? pack8(y1) : make_uint4(0, 0, 0, 0);
+      uint4 o0 = make_uint4(0, 0, 0, 0), o1 = make_uint4(0, 0, 0, 0);
+      if (valid) {
+        o0 = make_uint4(HB_BAND_PACK(y0[0], y0[1]), HB_BAND_PACK(y0[2], y0[3]), HB_BAND_PACK(y0[4], y0[5]),
+                        HB_BAND_PACK(y0[6], y0[7]));
+        o1 = make_uint4(HB_BAND_PACK(y1[0], y1[1]), HB_BAND_PACK(y1[2], y1[3]), HB_BAND_PACK(y1[4], y1[5]),
+                        HB_BAND_PACK(y1[6], y1[7]));
+      }
+      *p0 = o0;
+      *p1 = o1;
     }
   }
 }
@@ -205,55 +270,50 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw + 1023u) & ~1023u) - raw);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBars);
-  uint64_t* q_full = bars + 0;    // [2] 4 prep-warp arrivals (prepared q, q_diff)
-  uint64_t* q_empty = bars + 2;   // [2] commit (last S MMA of the unit)
-  uint64_t* k_full = bars + 4;    // [3] 4 prep-warp arrivals (prepared k, k_diff; v landed)
-  uint64_t* k_empty = bars + 7;   // [3] commit (last PV_B of the tile)
-  uint64_t* s_full = bars + 10;   // [2] commit
-  uint64_t* p_ready = bars + 12;  // [2] 4 softmax warps
-  uint64_t* o_full = bars + 14;   // [2] commit
-  uint64_t* o_empty = bars + 16;  // [2] 4 epilogue warps
-  uint64_t* sa_full = bars + 18;  // [2] 4 branch-A warps
-  uint64_t* drain = bars + 20;
-  uint64_t* q_raw = bars + 21;    // [2] TMA bytes of raw q, q_diff
-  uint64_t* k_raw = bars + 23;    // [3] TMA bytes of raw k, k_diff, v
+  uint64_t* q_raw = bars + 0;     // [2] TMA bytes of raw q, q_diff
+  uint64_t* q_full = bars + 2;    // [2] prep-warp arrivals (prepared q, q_diff)
+  uint64_t* q_empty = bars + 4;   // [2] commit after the unit's last S MMA
+  uint64_t* k_raw = bars + 6;     // [3] TMA bytes of raw k, k_diff, v
+  uint64_t* k_full = bars + 9;    // [3] prep-warp arrivals (prepared k, k_diff; v landed)
+  uint64_t* k_empty = bars + 12;  // [3] commit after the tile's last P V
+  uint64_t* s_full = bars + 15;   // [branch] commit after S_X(t)
+  uint64_t* s_free = bars + 17;   // [branch] 4 softmax warps: S_X(t) is in registers
+  uint64_t* p_ready = bars + 19;  // [branch] 4 softmax warps: P_X(t) written, O_X rescaled
+  uint64_t* o_done = bars + 21;   // [branch] commit after PV_X(t)
+  uint64_t* o_full = bars + 23;   // commit after the unit's last PV_B (both O final)
+  uint64_t* o_free = bars + 24;   // 4 epilogue warps: O loaded
+  uint64_t* sc_full = bars + 25;  // [unit parity] 8 softmax warps: 1 / l_A, lambda / l_B written
+  uint64_t* drain = bars + 27;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kOffMisc + 4);
+  // norms: alpha at index 3 of each 132-float row so gamma (index 4) and beta (index 68) start 16-byte aligned
   float* norms = reinterpret_cast<float*>(smem + kOffNorm);
-  float* scale_a = reinterpret_cast<float*>(smem + kOffScaleA);
+  float* scale = reinterpret_cast<float*>(smem + kOffScale);
   float* freqs = reinterpret_cast<float*>(smem + kOffFreq);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const long long t0 = clock64();
-  (void)t0;
-#ifdef HB_TRACE
-  unsigned* trace_buf = reinterpret_cast<unsigned*>(smem + kOffTrace);
-  int trace_n = 0, trace_slot = -1;
-#endif
   const int u0 = (int)(((long long)blockIdx.x * p.units) / gridDim.x);
   const int u1 = (int)(((long long)(blockIdx.x + 1) * p.units) / gridDim.x);
   const int nunits = u1 - u0;
 
-#ifdef HB_TRACE
-  if (threadIdx.x < kTraceSlots) trace_buf[2 * kTraceSlots * kTraceEvents + threadIdx.x] = 0;
-#endif
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) {
+      mbar_init(&q_raw[i], 1);
       mbar_init(&q_full[i], kPrepWarps);
       mbar_init(&q_empty[i], 1);
       mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 4);
       mbar_init(&p_ready[i], 4);
-      mbar_init(&o_full[i], 1);
-      mbar_init(&o_empty[i], 4);
-      mbar_init(&sa_full[i], 4);
+      mbar_init(&o_done[i], 1);
+      mbar_init(&sc_full[i], 8);
     }
     for (int i = 0; i < kSlots; ++i) {
+      mbar_init(&k_raw[i], 1);
       mbar_init(&k_full[i], kPrepWarps);
       mbar_init(&k_empty[i], 1);
-      mbar_init(&k_raw[i], 1);
     }
-    mbar_init(&q_raw[0], 1);
-    mbar_init(&q_raw[1], 1);
+    mbar_init(o_full, 1);
+    mbar_init(o_free, 4);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -261,7 +321,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   for (int i = threadIdx.x; i < 2 * kNormStride; i += kThreads) {
     const int which = i / kNormStride, k = i - which * kNormStride;
-    norms[i] = k < 129 ? (which ? p.k_norm : p.q_norm)[k] : 0.f;
+    norms[i] = (k >= 3 && k < 132) ? (which ? p.k_norm : p.q_norm)[k - 3] : 0.f;
   }
   if (threadIdx.x < 32) freqs[threadIdx.x] = threadIdx.x < p.half ? p.inv_freq[threadIdx.x] : 0.f;
   if (warp == 1) {
@@ -275,6 +335,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0) {
     // ---------------------------------------------------------------- TMA producer (raw tiles)
+    regs_dec<kRegsOther>();
     if (lane == 0) {
       Sched sch;
       int kissued = 0, qissued = 0;
@@ -283,29 +344,32 @@ __global__ void __launch_bounds__(kThreads, 1)
         sch.advance(x, p.heads);
         const int col = (p.head0 + x.h) * kHeadDim, sec = p.H_total * kHeadDim;
         const int qb = j & 1;
-        if (j >= 2 && !mbar_wait(&q_empty[qb], ((j >> 1) & 1) ^ 1)) {
+        if (j >= 2 && !slack_wait(&q_empty[qb], ((j >> 1) & 1) ^ 1)) {
           *abort_flag = 1;
           break;
         }
         uint8_t* qdst = smem + kOffQ + qb * kQBytes;
-        TRACE(0, 100 + j, t0);
         mbar_arrive_expect_tx(&q_raw[qb], 2 * kTileBytes);
         tma_load_3d(qdst, &tmap, col, x.qt * kTileRows, x.b, &q_raw[qb]);
         tma_load_3d(qdst + kTileBytes, &tmap, 3 * sec + col, x.qt * kTileRows, x.b, &q_raw[qb]);
         qissued = j + 1;
+        bool fail = false;
         for (int kt = sch.first_new; kt <= x.khi; ++kt) {
           const int s = sch.seq(kt), slot = s % kSlots;
-          if (s >= kSlots && !mbar_wait(&k_empty[slot], ((s / kSlots) & 1) ^ 1)) {
-            *abort_flag = 1;
+          if (s >= kSlots && !slack_wait(&k_empty[slot], ((s / kSlots) & 1) ^ 1)) {
+            fail = true;
             break;
           }
           uint8_t* kdst = smem + slot * kSlotBytes;
-          TRACE(0, 200 + kt, t0);
           mbar_arrive_expect_tx(&k_raw[slot], 3 * kTileBytes);
           tma_load_3d(kdst, &tmap, sec + col, kt * kTileRows, x.b, &k_raw[slot]);
           tma_load_3d(kdst + kTileBytes, &tmap, 4 * sec + col, kt * kTileRows, x.b, &k_raw[slot]);
           tma_load_3d(kdst + 2 * kTileBytes, &tmap, 2 * sec + col, kt * kTileRows, x.b, &k_raw[slot]);
           kissued = s + 1;
+        }
+        if (fail) {
+          *abort_flag = 1;
+          break;
         }
       }
       // drain: every copy issued into this CTA's shared memory lands before it exits
@@ -314,144 +378,157 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
+    regs_dec<kRegsOther>();
     if (lane == 0) {
       constexpr uint32_t idS = idesc_bf16_f32(128, 128, false);
       constexpr uint32_t idO = idesc_bf16_f32(128, 64, true);
-      const uint32_t tSa = tmem, tSb = tmem + 128;
       const uint32_t qbase = smem_u32(smem + kOffQ), kbase = smem_u32(smem);
+      // Key tile t of the flat list: its unit, ring slot, place in the unit and whether its slot is released
+      // after its P V (no later unit of this run reads the same key tile).
+      struct Tile {
+        int j, qb, slot, first, last, rel;
+      };
       Sched sch;
       bool ok = true;
-      int t = 0;
-      // pending PV_B: tile counter, slot, O buffer, accumulate, last tile of its unit, release its slot
-      int pb_t = -1, pb_slot = 0, pb_ob = 0, pb_acc = 0, pb_last = 0, pb_rel = 0;
-      auto issue_pv_b = [&]() -> bool {
-        if (!mbar_wait(&p_ready[1], pb_t & 1)) return false;
-        tc_fence_after();
-        const uint32_t vb = kbase + pb_slot * kSlotBytes + 2 * kTileBytes;
-        const uint32_t tO = tmem + 320 + 128 * pb_ob;
-#pragma unroll
-        for (int k = 0; k < 8; ++k) mma_bf16_ts(tO, tSb + 8 * k, smem_desc_sw128(vb + 2048 * k), idO, (pb_acc || k > 0));
-        if (pb_last) tc_commit(&o_full[pb_ob]);
-        if (pb_rel) tc_commit(&k_empty[pb_slot]);
-        pb_t = -1;
+      int j = -1, kt = 0, khi = -1;
+      Unit cur{}, nx{};
+      if (nunits > 0) nx = decode(p, u0);
+      // next tile of the flat list (advancing the unit when the current one is exhausted); false at the end
+      auto next_tile = [&](Tile& tl) -> bool {
+        if (kt > khi) {
+          if (j + 1 >= nunits) return false;
+          ++j;
+          cur = nx;
+          if (j + 1 < nunits) nx = decode(p, u0 + j + 1);
+          sch.advance(cur, p.heads);
+          kt = cur.klo;
+          khi = cur.khi;
+        }
+        const int s = sch.seq(kt);
+        tl.j = j;
+        tl.qb = j & 1;
+        tl.slot = s % kSlots;
+        tl.first = kt == cur.klo;
+        tl.last = kt == cur.khi;
+        tl.rel = !(j + 1 < nunits && same_run(cur, nx) && kt >= nx.klo);
+        // a key tile not loaded before this unit waits for its preparation
+        if (kt >= sch.first_new) {
+          if (!mma_wait(&k_full[tl.slot], (s / kSlots) & 1) || *abort_flag) ok = false;
+        }
+        ++kt;
         return true;
       };
-      Unit nx = nunits > 0 ? decode(p, u0) : Unit{};
-      for (int j = 0; ok && j < nunits; ++j) {
-        const Unit x = nx;
-        const bool has_next = j + 1 < nunits;
-        if (has_next) nx = decode(p, u0 + j + 1);
-        sch.advance(x, p.heads);
-        const int qb = j & 1;
-        if (!mbar_wait(&q_full[qb], (j >> 1) & 1) || *abort_flag) {
+      auto issue_s = [&](const Tile& tl, int t) {
+        if (tl.first && (!mma_wait(&q_full[tl.qb], (tl.j >> 1) & 1) || *abort_flag)) {
           ok = false;
-          break;
+          return;
         }
-        tc_fence_after();
-        TRACE(1, 100 + j, t0);
-        const uint32_t qa = qbase + qb * kQBytes, qd = qa + kTileBytes;
-        for (int kt = x.klo; kt <= x.khi; ++kt) {
-          const int i = kt - x.klo;
-          const int s = sch.seq(kt), slot = s % kSlots;
-          if (kt >= sch.first_new) {
-            if (!mbar_wait(&k_full[slot], (s / kSlots) & 1) || *abort_flag) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-          }
-          TRACE(1, 200 + kt, t0);
-          const uint32_t kb = kbase + slot * kSlotBytes;
-#pragma unroll
-          for (int k = 0; k < 4; ++k)
-            mma_bf16_ss(tSa, smem_desc_sw128(qa + 32 * k), smem_desc_sw128(kb + 32 * k), idS, k > 0);
-          tc_commit(&s_full[0]);
-          TRACE(1, 500 + kt, t0);
-          if (pb_t >= 0 && !issue_pv_b()) {
+        const uint32_t qa = qbase + tl.qb * kQBytes;
+        const uint32_t kb = kbase + tl.slot * kSlotBytes;
+#pragma unroll 1
+        for (int x = 0; x < 2; ++x) {
+          if (t > 0 && !mma_wait(&s_free[x], (t - 1) & 1)) {  // the softmax has loaded S_X(t - 1)
             ok = false;
-            break;
+            return;
           }
-          TRACE(1, 600 + kt, t0);
-#pragma unroll
-          for (int k = 0; k < 4; ++k)
-            mma_bf16_ss(tSb, smem_desc_sw128(qd + 32 * k), smem_desc_sw128(kb + kTileBytes + 32 * k), idS, k > 0);
-          tc_commit(&s_full[1]);
-          if (kt == x.khi) tc_commit(&q_empty[qb]);
-          if (i == 0 && j >= 2 && !mbar_wait(&o_empty[qb], ((j >> 1) & 1) ^ 1)) {
-            ok = false;
-            break;
-          }
-          TRACE(1, 300 + kt, t0);
-          if (!mbar_wait(&p_ready[0], t & 1)) {
-            ok = false;
-            break;
-          }
-          TRACE(1, 400 + kt, t0);
           tc_fence_after();
-          const uint32_t vb = kb + 2 * kTileBytes;
-          const uint32_t tOa = tmem + 256 + 128 * qb;
+          const uint32_t qx = qa + x * kTileBytes, kx = kb + x * kTileBytes;
+          const uint32_t tS = tmem + kColS + 128u * x;
+#pragma unroll
+          for (int k = 0; k < 4; ++k) mma_bf16_ss(tS, smem_desc_sw128(qx + 32 * k), smem_desc_sw128(kx + 32 * k), idS, k > 0);
+          tc_commit(&s_full[x]);
+        }
+        if (tl.last) tc_commit(&q_empty[tl.qb]);
+      };
+      auto issue_pv = [&](const Tile& tl, int t) {
+        if (tl.first && tl.j > 0 && !mma_wait(o_free, (tl.j - 1) & 1)) {  // the epilogue has loaded O of unit j-1
+          ok = false;
+          return;
+        }
+        const uint32_t vb = kbase + tl.slot * kSlotBytes + 2 * kTileBytes;
+#pragma unroll 1
+        for (int x = 0; x < 2; ++x) {
+          if (!mma_wait(&p_ready[x], t & 1)) {
+            ok = false;
+            return;
+          }
+          tc_fence_after();
+          const uint32_t tP = tmem + kColP + 64u * x, tO = tmem + kColO + 64u * x;
 #pragma unroll
           for (int k = 0; k < 8; ++k)
-            mma_bf16_ts(tOa, tSa + 8 * k, smem_desc_sw128(vb + 2048 * k), idO, (i > 0 || k > 0));
-          pb_t = t;
-          pb_slot = slot;
-          pb_ob = qb;
-          pb_acc = i > 0;
-          pb_last = kt == x.khi;
-          pb_rel = !(has_next && same_run(x, nx) && kt >= nx.klo);
-          ++t;
+            mma_bf16_ts(tO, tP + 8 * k, smem_desc_sw128(vb + 2048 * k), idO, (!tl.first || k > 0));
+          tc_commit(&o_done[x]);
         }
+        if (tl.last) tc_commit(o_full);
+        if (tl.rel) tc_commit(&k_empty[tl.slot]);
+      };
+      Tile cur_t{}, nxt_t{};
+      bool have = next_tile(cur_t);
+      if (have && ok) issue_s(cur_t, 0);
+      for (int t = 0; have && ok; ++t) {
+        const bool more = next_tile(nxt_t);
+        if (!ok) break;
+        if (more) {
+          issue_s(nxt_t, t + 1);
+          if (!ok) break;
+        }
+        issue_pv(cur_t, t);
+        cur_t = nxt_t;
+        have = more;
       }
-      if (ok && pb_t >= 0) ok = issue_pv_b();
       if (!ok) *abort_flag = 1;
       tc_commit(drain);
       mbar_wait(drain, 0);
     }
   } else if (warp >= 4 && warp < 12) {
-    // ---------------------------------------------------------------- softmax (+ epilogue in branch B)
+    // ---------------------------------------------------------------- softmax (one query row per thread)
+    regs_inc<kRegsSoftmax>();
     const int br = (warp - 4) >> 2;
     const int quad = warp & 3;
     const int row = quad * 32 + lane;
     const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
-    const uint32_t tS = tmem + lane_base + (br ? 128u : 0u);
+    const uint32_t tS = tmem + lane_base + kColS + 128u * br;
+    const uint32_t tP = tmem + lane_base + kColP + 64u * br;
+    const uint32_t tO = tmem + lane_base + kColO + 64u * br;
     int t = 0;
     bool ok = true;
     for (int j = 0; ok && j < nunits; ++j) {
       const Unit x = decode(p, u0 + j);
-      const int ob = j & 1;
-      const uint32_t tO = tmem + lane_base + 256u + 128u * ob + (br ? 64u : 0u);
       const int q = x.qt * kTileRows + row;
-      const int qw_lo = x.qt * kTileRows + quad * 32, qw_hi = qw_lo + 31;
+      const int qw_lo = x.qt * kTileRows + quad * 32;
       float m = -INFINITY, l = 0.f;
       for (int kt = x.klo; kt <= x.khi; ++kt, ++t) {
-        if (!(ok = warp_wait(&s_full[br], t & 1, abort_flag))) break;
-        if (lane == 0 && quad == 0) TRACE(2 + br, 100 + kt, t0);
+        if (!(ok = __all_sync(0xffffffffu, soft_wait(&s_full[br], t & 1) && !*abort_flag))) break;
         tc_fence_after();
         const int k0 = kt * kTileRows;
-        // pass 1: row max over in-band keys; 32-key chunks outside the band for the whole warp are skipped,
-        // chunks inside it for every lane of the warp need no mask (two chains of three-input maxima)
-        float mx0 = -INFINITY, mx1 = -INFINITY;
-        uint32_t r[32];
-#pragma unroll 1
+        // the tile's 128 scores with four loads in flight and one wait; then S may be overwritten
+        uint32_t r[4][32];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) tmem_ld32(tS + 32 * c, r[c]);
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s_free[br]);
+        // keys outside the band of this row (or past the buffer) -> -inf; row max in four chains of three-input
+        // maxima (the scale is positive, so it commutes with the max)
+        float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
         for (int c = 0; c < 4; ++c) {
           const int kc = k0 + 32 * c;
-          if (kc >= p.rows || kc > qw_hi + p.window || kc + 31 < qw_lo - p.window) continue;
           const uint32_t bits = band_bits(kc, q, p.window, p.rows);
-          tmem_ld32(tS + 32 * c, r);
-          tmem_wait_ld();
           if (!__all_sync(0xffffffffu, bits == 0xffffffffu)) {
 #pragma unroll
             for (int e = 0; e < 32; ++e)
-              if (!((bits >> e) & 1u)) r[e] = 0xff800000u;  // -inf
+              if (!((bits >> e) & 1u)) r[c][e] = 0xff800000u;  // -inf
           }
 #pragma unroll
-          for (int e = 0; e < 32; e += 4) {
-            mx0 = fmax3(mx0, __uint_as_float(r[e]), __uint_as_float(r[e + 1]));
-            mx1 = fmax3(mx1, __uint_as_float(r[e + 2]), __uint_as_float(r[e + 3]));
+          for (int e = 0; e < 32; e += 8) {
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+              mx[u] = fmax3(mx[u], __uint_as_float(r[c][e + 2 * u]), __uint_as_float(r[c][e + 2 * u + 1]));
           }
         }
-        if (lane == 0 && quad == 0) TRACE(2 + br, 500 + kt, t0);
-        const float rmax = fmaxf(mx0, mx1) * kScoreScale;
+        const float rmax = fmaxf(fmax3(mx[0], mx[1], mx[2]), mx[3]) * kScoreScale;
         const float m_new = fmaxf(m, rmax);
         const bool upd = m_new > m + kRescaleThreshold;
         float alpha = 1.f;
@@ -460,48 +537,41 @@ __global__ void __launch_bounds__(kThreads, 1)
           m = m_new;
         }
         const float nm = (m == -INFINITY) ? 0.f : -m;
-        // pass 2: P = exp2(s * scale - m) as bf16 into the first 64 columns of S (in place); packed FMA per key
-        // pair and two packed row-sum accumulators
-        float rs0 = 0.f, rs1 = 0.f, rs2 = 0.f, rs3 = 0.f;
-#pragma unroll 1
+        // P = exp2(s * scale - m) as bf16 pairs: packed FMA per key pair, the row sum in packed accumulators;
+        // chunks with no in-band key for the warp are zero
+        float rs[4] = {0.f, 0.f, 0.f, 0.f};
+        uint32_t pk[4][16];  // packed key pairs of each chunk
+#pragma unroll
         for (int c = 0; c < 4; ++c) {
-          const int kc = k0 + 32 * c;
-          uint32_t pk[16];
-          if (kc >= p.rows || kc > qw_hi + p.window || kc + 31 < qw_lo - p.window) {
+          if (!chunk_live(k0 + 32 * c, qw_lo, p.window, p.rows)) {
 #pragma unroll
-            for (int e = 0; e < 16; ++e) pk[e] = 0u;
-          } else {
-            const uint32_t bits = band_bits(kc, q, p.window, p.rows);
-            tmem_ld32(tS + 32 * c, r);
-            tmem_wait_ld();
-            if (!__all_sync(0xffffffffu, bits == 0xffffffffu)) {
-#pragma unroll
-              for (int e = 0; e < 32; ++e)
-                if (!((bits >> e) & 1u)) r[e] = 0xff800000u;
-            }
-#pragma unroll
-            for (int e = 0; e < 16; ++e) {
-              float x0, x1;
-              ffma2(x0, x1, __uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1]), kScoreScale, kScoreScale, nm, nm);
-              float p0, p1;
-              if ((e & kPolyMask) == kPolyMask) {  // a share of the exponentials on the FMA pipe
-                exp2_poly2(x0, x1, p0, p1);
-              } else {
-                p0 = ex2_approx(x0);
-                p1 = ex2_approx(x1);
-              }
-              if (e & 1)
-                fadd2(rs2, rs3, rs2, rs3, p0, p1);
-              else
-                fadd2(rs0, rs1, rs0, rs1, p0, p1);
-              pk[e] = pack_bf16x2(p0, p1);
-            }
+            for (int e = 0; e < 16; ++e) pk[c][e] = 0u;
+            continue;
           }
-          tmem_st16(tS + 16 * c, pk);
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            float x0, x1;
+            ffma2(x0, x1, __uint_as_float(r[c][2 * e]), __uint_as_float(r[c][2 * e + 1]), kScoreScale, kScoreScale,
+                  nm, nm);
+            float p0, p1;
+            if ((e & kPolyMask) == kPolyMask) {  // a share of the exponentials on the FMA pipe
+              exp2_poly2(x0, x1, p0, p1);
+            } else {
+              p0 = ex2_approx(x0);
+              p1 = ex2_approx(x1);
+            }
+            const int a = (e & 1) * 2;
+            fadd2(rs[a], rs[a + 1], rs[a], rs[a + 1], p0, p1);
+            pk[c][e] = HB_BAND_PACK(p0, p1);
+          }
         }
-        const float rs = (rs0 + rs1) + (rs2 + rs3);
-        l = l * alpha + rs;
-        if (lane == 0 && quad == 0) TRACE(2 + br, 600 + kt, t0);
+        l = l * alpha + ((rs[0] + rs[1]) + (rs[2] + rs[3]));
+        if (t > 0) {  // the previous P V of this branch has read P and landed in O
+          if (!(ok = __all_sync(0xffffffffu, soft_wait(&o_done[br], (t - 1) & 1)))) break;
+          tc_fence_after();
+        }
+#pragma unroll
+        for (int c = 0; c < 4; ++c) tmem_st16(tP + 16 * c, pk[c]);
         if (kt > x.klo && __any_sync(0xffffffffu, upd)) {
           uint32_t o[32];
 #pragma unroll 1
@@ -517,118 +587,94 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&p_ready[br]);
-        if (lane == 0 && quad == 0) TRACE(2 + br, 200 + kt, t0);
       }
       if (!ok) break;
-      if (br == 0) {
-        scale_a[ob * kTileRows + row] = 1.f / l;
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&sa_full[ob]);
-        continue;
-      }
-      // branch B: epilogue of unit j once both O accumulators are final
-      if (!(ok = warp_wait(&o_full[ob], (j >> 1) & 1, abort_flag))) break;
+      // the epilogue's per-row factors: 1 / l_A and lambda / l_B (each branch normalised after P V)
+      scale[((j & 1) * 2 + br) * kTileRows + row] = (br ? (p.lam ? p.lam[p.lam_pair0 + x.h / 2] : 1.f) : 1.f) / l;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sc_full[j & 1]);
+    }
+  } else {
+    // ---------------------------------------------------------------- preparation (warps 2-3, 12-15) + epilogue (12-15)
+    regs_dec<kRegsOther>();
+    const bool epi = warp >= 12;
+    const int pt = epi ? threadIdx.x - 10 * 32 : threadIdx.x - 2 * 32;
+    const int quad = warp & 3;
+    const int row = quad * 32 + lane;
+    const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
+    bool ok = true;
+    // epilogue of unit jj: out = O_A * (1 / l_A) - O_B * (lambda / l_B) in fp32, one bf16 cast
+    auto epilogue = [&](int jj) {
+      const Unit x = decode(p, u0 + jj);
+      if (!(ok = warp_slack_wait(o_full, jj & 1, abort_flag))) return;
       tc_fence_after();
-      if (!(ok = warp_wait(&sa_full[ob], (j >> 1) & 1, abort_flag))) break;
-      if (lane == 0 && quad == 0) TRACE(3, 300 + j, t0);
-      const float inv_a = scale_a[ob * kTileRows + row];
-      const float sb = (p.lam ? p.lam[p.lam_pair0 + x.h / 2] : 1.f) / l;
+      if (!(ok = warp_wait(&sc_full[jj & 1], (jj >> 1) & 1, abort_flag))) return;
+      const float inv_a = scale[((jj & 1) * 2) * kTileRows + row];
+      const float sb = scale[((jj & 1) * 2 + 1) * kTileRows + row];
+      const int q = x.qt * kTileRows + row;
       const bool store = q >= p.q_begin && q < p.q_begin + p.q_count;
-      uint16_t* dst = p.out + ((size_t)x.b * p.q_count + (q - p.q_begin)) * p.out_row_stride + (size_t)x.h * kHeadDim;
-      const uint32_t tOa = tmem + lane_base + 256u + 128u * ob;
+      uint16_t* dst = p.out + ((size_t)x.b * p.q_count + (store ? q - p.q_begin : 0)) * p.out_row_stride +
+                      (size_t)x.h * kHeadDim;
+      const uint32_t tOa = tmem + lane_base + kColO, tOb = tOa + 64u;
 #pragma unroll 1
-      for (int c = 0; c < 2; ++c) {
-        uint32_t oa[32], obv[32];
-        tmem_ld32(tOa + 32 * c, oa);
-        tmem_ld32(tO + 32 * c, obv);
+      for (int c = 0; c < 4; ++c) {
+        uint32_t oa[16], ob[16];
+        tmem_ld16(tOa + 16 * c, oa);
+        tmem_ld16(tOb + 16 * c, ob);
         tmem_wait_ld();
+        if (c == 3) {  // O is in registers: the next unit's first P V may overwrite it
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(o_free);
+        }
+        uint32_t w[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float y0 = __fmul_rn(__uint_as_float(oa[2 * e]), inv_a) - __fmul_rn(__uint_as_float(ob[2 * e]), sb);
+          const float y1 =
+              __fmul_rn(__uint_as_float(oa[2 * e + 1]), inv_a) - __fmul_rn(__uint_as_float(ob[2 * e + 1]), sb);
+          w[e] = pack_bf16x2(y0, y1);
+        }
         if (store) {
-          uint32_t w[16];
-#pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            const float y0 = __fmul_rn(__uint_as_float(oa[2 * e]), inv_a) - __fmul_rn(__uint_as_float(obv[2 * e]), sb);
-            const float y1 =
-                __fmul_rn(__uint_as_float(oa[2 * e + 1]), inv_a) - __fmul_rn(__uint_as_float(obv[2 * e + 1]), sb);
-            w[e] = pack_bf16x2(y0, y1);
-          }
-          uint4* d4 = reinterpret_cast<uint4*>(dst + 32 * c);
-#pragma unroll
-          for (int e = 0; e < 4; ++e) d4[e] = make_uint4(w[4 * e], w[4 * e + 1], w[4 * e + 2], w[4 * e + 3]);
+          uint4* d4 = reinterpret_cast<uint4*>(dst + 16 * c);
+          d4[0] = make_uint4(w[0], w[1], w[2], w[3]);
+          d4[1] = make_uint4(w[4], w[5], w[6], w[7]);
         }
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&o_empty[ob]);
-    }
-  } else if (warp >= 12 || warp == 2 || warp == 3) {
-    // ---------------------------------------------------------------- preparation (in place: DyT + RoPE -> bf16)
-    const int pt = warp >= 12 ? threadIdx.x - 10 * 32 : threadIdx.x - 2 * 32;
+    };
     Sched sch;
-    // one job list (q tile of unit j, then its new key tiles) so the transform is instantiated once
-    int j = -1, kt = 0, khi = -1, qt = 0;
-    bool q_job = false;
-    while (true) {
-      if (!q_job && kt > khi) {  // next unit
-        if (++j >= nunits) break;
-        const Unit x = decode(p, u0 + j);
-        sch.advance(x, p.heads);
-        kt = sch.first_new;
-        khi = x.khi;
-        qt = x.qt;
-        q_job = true;
-      }
-      uint64_t* raw_bar;
-      uint64_t* full_bar;
-      uint32_t parity;
-      uint8_t* dst;
-      const float* nrm;
-      int tile;
-      if (q_job) {
-        const int qb = j & 1;
-        raw_bar = &q_raw[qb];
-        full_bar = &q_full[qb];
-        parity = (j >> 1) & 1;
-        dst = smem + kOffQ + qb * kQBytes;
-        nrm = norms;
-        tile = qt;
-        q_job = false;
-      } else {
-        const int s = sch.seq(kt), slot = s % kSlots;
-        raw_bar = &k_raw[slot];
-        full_bar = &k_full[slot];
-        parity = (s / kSlots) & 1;
-        dst = smem + slot * kSlotBytes;
-        nrm = norms + kNormStride;
-        tile = kt++;
-      }
-      if (!warp_wait(raw_bar, parity, abort_flag)) break;
-      if (pt == 0) TRACE(4, 100 + tile, t0);
-      prep_inplace(p, tile, nrm, freqs, dst, dst + kTileBytes, pt, kPrepThreads);
-      if (pt == 0) TRACE(4, 200 + tile, t0);
+#pragma unroll 1
+    for (int j = 0; ok && j < nunits; ++j) {
+      const Unit x = decode(p, u0 + j);
+      sch.advance(x, p.heads);
+      // the unit's q tile, then its new key tiles; then (warps 12-15) the epilogue of the previous unit
+      const int qb = j & 1;
+      if (!(ok = warp_slack_wait(&q_raw[qb], (j >> 1) & 1, abort_flag))) break;
+      uint8_t* qdst = smem + kOffQ + qb * kQBytes;
+      prep_inplace(p, x.qt, norms, freqs, qdst, qdst + kTileBytes, pt, kPrepThreads);
       fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) mbar_arrive(full_bar);
+      if (lane == 0) mbar_arrive(&q_full[qb]);
+#pragma unroll 1
+      for (int kt = sch.first_new; kt <= x.khi; ++kt) {
+        const int s = sch.seq(kt), slot = s % kSlots;
+        if (!(ok = warp_slack_wait(&k_raw[slot], (s / kSlots) & 1, abort_flag))) break;
+        uint8_t* kdst = smem + slot * kSlotBytes;
+        prep_inplace(p, kt, norms + kNormStride, freqs, kdst, kdst + kTileBytes, pt, kPrepThreads);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&k_full[slot]);
+      }
+      if (ok && epi && j > 0) epilogue(j - 1);
     }
+    if (ok && epi && nunits > 0) epilogue(nunits - 1);
   }
-#ifdef HB_TRACE
-  if (trace_slot >= 0) trace_buf[2 * kTraceSlots * kTraceEvents + trace_slot] = trace_n;
-#endif
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
-#ifdef HB_TRACE
-  if (blockIdx.x == 0) {
-    for (int i = threadIdx.x; i < kTraceSlots * kTraceEvents; i += kThreads) {
-      const int sl = i / kTraceEvents, e = i - sl * kTraceEvents;
-      g_trace[sl][2 * e] = trace_buf[2 * i];
-      g_trace[sl][2 * e + 1] = trace_buf[2 * i + 1];
-    }
-    if (threadIdx.x < kTraceSlots) g_trace_n[threadIdx.x] = trace_buf[2 * kTraceSlots * kTraceEvents + threadIdx.x];
-  }
-#endif
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -645,17 +691,13 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 }  // namespace
 
-#ifdef HB_TRACE
-extern "C" int hb_debug_trace(unsigned int* out, int reset) {
-  if (cudaMemcpyFromSymbol(out, g_trace, sizeof(g_trace)) != cudaSuccess) return 1;
-  if (cudaMemcpyFromSymbol(out + 8 * 2048, g_trace_n, sizeof(g_trace_n)) != cudaSuccess) return 1;
-  if (reset) {
-    unsigned int z[8] = {};
-    if (cudaMemcpyToSymbol(g_trace_n, z, sizeof(z)) != cudaSuccess) return 1;
-  }
-  return 0;
+int band_fused_take_status(unsigned int* status) {
+  unsigned int v = 0, zero = 0;
+  if (cudaMemcpyFromSymbol(&v, g_device_status_local, sizeof(v)) != cudaSuccess) return HB_ERR_LAUNCH;
+  if (v && cudaMemcpyToSymbol(g_device_status_local, &zero, sizeof(zero)) != cudaSuccess) return HB_ERR_LAUNCH;
+  *status = v;
+  return HB_OK;
 }
-#endif
 
 int band_fused_attend(const BandFusedParams& p, cudaStream_t stream) {
   auto encode = encode_fn();
@@ -675,6 +717,11 @@ int band_fused_attend(const BandFusedParams& p, cudaStream_t stream) {
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   static bool configured[64] = {};
   if (dev < 64 && !configured[dev]) {
+    // The warpgroups' setmaxnreg split assumes the block is launched with exactly 128 registers per thread;
+    // with any other count the register increase could never be granted, so refuse to launch.
+    cudaFuncAttributes attr{};
+    if (cudaFuncGetAttributes(&attr, band_fused_kernel) != cudaSuccess || attr.numRegs != kLaunchRegs)
+      return HB_ERR_LAUNCH;
     if (cudaFuncSetAttribute(band_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) != cudaSuccess)
       return HB_ERR_LAUNCH;
     configured[dev] = true;

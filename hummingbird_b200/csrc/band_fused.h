@@ -26,4 +26,8 @@ constexpr int kFusedMaxWindow = 128;
 
 int band_fused_attend(const BandFusedParams& p, cudaStream_t stream);
 
+// Read (and clear, when set) the status word of the fused band kernel's translation unit on the current
+// device; an HbStatus.
+int band_fused_take_status(unsigned int* status);
+
 }  // namespace hb

@@ -189,12 +189,13 @@ extern "C" int hb_dense_workspace_bytes(int batch, int length, int pair_count, s
   return HB_OK;
 }
 
-extern "C" int hb_dense_diff_attn(const void* qkv, int64_t qkv_row_stride, const float* q_weight,
-                                  const float* k_weight, const float* cos, const float* sin, int64_t table_stride,
-                                  const void* vmask, int64_t mask_batch_stride, int64_t mask_row_stride,
-                                  const float* lam, void* out, int64_t out_row_stride, int batch, int length,
-                                  int num_heads, int head_dim, int half, float eps, int pair_begin, int pair_count,
-                                  void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+namespace {
+
+// The host-side argument checks shared by both dense entry points (no device work, no workspace check).
+int dense_check_args(const void* qkv, int64_t qkv_row_stride, const float* q_weight, const float* k_weight,
+                     const float* cos, const float* sin, int64_t table_stride, const void* vmask, void* out,
+                     int64_t out_row_stride, int batch, int length, int num_heads, int head_dim, int half,
+                     int pair_begin, int pair_count) {
   if (!qkv || !q_weight || !k_weight || !cos || !sin || !vmask || !out) return HB_ERR_NULL;
   if (head_dim != kHeadDim || num_heads < 2 || num_heads % 2 || batch < 1 || length < 1) return HB_ERR_SHAPE;
   if (half < 8 || half > 32 || half % 8) return HB_ERR_SHAPE;
@@ -202,8 +203,22 @@ extern "C" int hb_dense_diff_attn(const void* qkv, int64_t qkv_row_stride, const
   if (qkv_row_stride < (int64_t)5 * num_heads * kHeadDim || table_stride < kHeadDim ||
       out_row_stride < (int64_t)2 * pair_count * kHeadDim)
     return HB_ERR_SHAPE;
-  if (!aligned16(qkv) || qkv_row_stride % 8 || !aligned16(out) || out_row_stride % 8 || !aligned16(workspace))
-    return HB_ERR_ALIGN;
+  if (!aligned16(qkv) || qkv_row_stride % 8 || !aligned16(out) || out_row_stride % 8) return HB_ERR_ALIGN;
+  return HB_OK;
+}
+
+}  // namespace
+
+extern "C" int hb_dense_diff_attn(const void* qkv, int64_t qkv_row_stride, const float* q_weight,
+                                  const float* k_weight, const float* cos, const float* sin, int64_t table_stride,
+                                  const void* vmask, int64_t mask_batch_stride, int64_t mask_row_stride,
+                                  const float* lam, void* out, int64_t out_row_stride, int batch, int length,
+                                  int num_heads, int head_dim, int half, float eps, int pair_begin, int pair_count,
+                                  void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  const int chk = dense_check_args(qkv, qkv_row_stride, q_weight, k_weight, cos, sin, table_stride, vmask, out,
+                                   out_row_stride, batch, length, num_heads, head_dim, half, pair_begin, pair_count);
+  if (chk != HB_OK) return chk;
+  if (!aligned16(workspace)) return HB_ERR_ALIGN;
   const int heads = 2 * pair_count;
   if (!workspace || workspace_bytes < prep_workspace_bytes(batch, length, heads)) return HB_ERR_WORKSPACE;
   int st = check_device();
@@ -268,7 +283,10 @@ int noalloc_scratch_address(void** out) {
   static std::atomic<void*> cache[64];
   void* ptr = cache[dev].load(std::memory_order_acquire);
   if (!ptr) {
-    if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || !ptr) return HB_ERR_LAUNCH;
+    if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || !ptr) {
+      cudaGetLastError();  // clear the failed lookup, so the next call does not report it as its own launch error
+      return HB_ERR_LAUNCH;
+    }
     cache[dev].store(ptr, std::memory_order_release);
   }
   *out = ptr;
@@ -293,9 +311,14 @@ extern "C" int hb_dense_diff_attn_noalloc(const void* qkv, int64_t qkv_row_strid
   if (batch < 1 || length < 1 || pair_count < 1) return HB_ERR_SHAPE;
   // refuse, before any device work, a problem whose prepared tiles would not fit the fixed scratch
   if (prep_workspace_bytes(batch, length, 2 * pair_count) > kNoAllocScratchBytes) return HB_ERR_WORKSPACE;
-  void* scratch = nullptr;
-  const int st = noalloc_scratch_address(&scratch);
+  // then the same host-side checks as the workspace entry point and the device check, so a bad argument or a
+  // non-sm_100 device is reported as such before the scratch lookup touches the device
+  int st = dense_check_args(qkv, qkv_row_stride, q_weight, k_weight, cos, sin, table_stride, vmask, out,
+                            out_row_stride, batch, length, num_heads, head_dim, half, pair_begin, pair_count);
   if (st != HB_OK) return st;
+  if ((st = check_device()) != HB_OK) return st;
+  void* scratch = nullptr;
+  if ((st = noalloc_scratch_address(&scratch)) != HB_OK) return st;
   return hb_dense_diff_attn(qkv, qkv_row_stride, q_weight, k_weight, cos, sin, table_stride, vmask, mask_batch_stride,
                             mask_row_stride, lam, out, out_row_stride, batch, length, num_heads, head_dim, half, eps,
                             pair_begin, pair_count, scratch, kNoAllocScratchBytes, stream);

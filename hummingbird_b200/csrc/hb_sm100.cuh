@@ -13,10 +13,19 @@
 
 namespace hb {
 
+#ifndef HB_WHOLE_PROGRAM
 // Library status word (per device): first error wins. Read and cleared by hb_device_status().
 extern __device__ unsigned int g_device_status;
 
 __device__ __forceinline__ void record_error(unsigned int code) { atomicCAS(&g_device_status, 0u, code); }
+#else
+// A translation unit compiled as whole-program device code (without -rdc, which ptxas needs to honour
+// setmaxnreg) cannot reach the library's status word in another unit: it keeps its own, which
+// hb_device_status() reads and clears together with the library's.
+static __device__ unsigned int g_device_status_local = 0;
+
+__device__ __forceinline__ void record_error(unsigned int code) { atomicCAS(&g_device_status_local, 0u, code); }
+#endif
 
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
@@ -61,6 +70,22 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsign
   while (true) {
     for (int i = 0; i < 64; ++i)
       if (mbar_try_wait(bar, parity)) return true;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      record_error(code);
+      return false;
+    }
+  }
+}
+
+// The same bounded wait for roles with slack (producers, preparation, epilogue): between polls the thread
+// sleeps for `sleep_ns`, leaving the issue slots of its SM sub-partition to the warps on the critical path.
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, unsigned sleep_ns,
+                                                unsigned int code = HB_ERR_TIMEOUT) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+    __nanosleep(sleep_ns);
+    if (mbar_try_wait(bar, parity)) return true;
     if (globaltimer_ns() - t0 > kWaitLimitNs) {
       record_error(code);
       return false;
@@ -305,6 +330,13 @@ __device__ __forceinline__ float tanh_approx(float x) {
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
+}
+// Two finite fp32 values -> packed bf16 pair by integer arithmetic: round to nearest with ties away from zero
+// (adding half a bf16 ulp to the magnitude bits), then the two high halves byte-permuted into one word. It
+// keeps the conversion off the XU pipe (where cvt.rn.bf16x2.f32 runs, next to ex2 / tanh / sin / cos) and
+// differs from round-to-nearest-even only on exact ties, one bf16 ulp apart.
+__device__ __forceinline__ uint32_t pack_bf16x2_int(float lo, float hi) {
+  return __byte_perm(__float_as_uint(lo) + 0x8000u, __float_as_uint(hi) + 0x8000u, 0x7632);
 }
 // Packed fp32 pairs (sm_100): one instruction for two lanes' worth of FMA / add / multiply.
 __device__ __forceinline__ void ffma2(float& d0, float& d1, float a0, float a1, float b0, float b1, float c0,

@@ -1,9 +1,9 @@
 """Fixed-shape calls of one hot-path kernel each, for profilers (`ncu -k <kernel> -s <skip> -c <count>`).
 
-    python -m hummingbird_b200.profile_cases band    # config 2: SAME-L band attention, B=1, L=82,688, 8 heads
-    python -m hummingbird_b200.profile_cases dense   # dense DiT self-attention, B=2, L=2,648, 16 heads
-    python -m hummingbird_b200.profile_cases cross   # DiT cross-attention, B=2, 2,648 queries, 128 context, 16 heads
-    python -m hummingbird_b200.profile_cases glue    # DiT row kernels: residual + RMSNorm + adaLN, GLU + int8
+    python profile_cases.py band    # config 2: SAME-L band attention, B=1, L=82,688, 8 heads
+    python profile_cases.py dense   # dense DiT self-attention, B=2, L=2,648, 16 heads
+    python profile_cases.py cross   # DiT cross-attention, B=2, 2,648 queries, 128 context, 16 heads
+    python profile_cases.py glue    # DiT row kernels: residual + RMSNorm + adaLN, GLU + int8
 
 Each case builds its seeded synthetic inputs (`hummingbird_b200.workloads`), makes `--calls` calls (default 3)
 on the current GPU and prints a checksum of the last output. Nothing is timed here: the bench times.
@@ -11,8 +11,12 @@ on the current GPU and prints a checksum of the last output. Nothing is timed he
 from __future__ import annotations
 
 import argparse
+import sys
+from pathlib import Path
 
 import torch
+
+sys.path.insert(0, str(Path(__file__).resolve().parent))
 
 
 def band(calls: int) -> torch.Tensor:

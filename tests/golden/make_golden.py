@@ -2,7 +2,7 @@
 
 JAX is not installable here, so `tests/golden/_jaxshim/jax` (a numpy stand-in for the few JAX calls on
 the reference's XLA path) is put on `sys.path` and the reference package `sa3jax` is imported from the
-reference checkout (`$HB_REFERENCE`, else the checkout's path in the build container). The reference then runs in fp32
+reference checkout named by `$HB_REFERENCE` (required). The reference then runs in fp32
 (`dtypes.FP32_PARITY`) through its own functions:
 
 * dense: `sa3jax.dit._self_attention` (dit.py:185-200) with `DiTConfig(attention="xla", differential=True)`,
@@ -17,7 +17,7 @@ reference checkout (`$HB_REFERENCE`, else the checkout's path in the build conta
 * w8a8: no reference exists; the accumulators come from a pure-Python integer dot product, independent
   of the numpy oracle.
 
-Run from the repo root:  python tests/golden/make_golden.py
+Run from the repo root:  HB_REFERENCE=<path of a hummingbird checkout> python tests/golden/make_golden.py
 This script (and only this script) reads the reference; the fixtures it writes are what tests use.
 """
 from __future__ import annotations
@@ -33,7 +33,9 @@ ROOT = HERE.parents[1]
 
 
 def _import_reference():
-    ref = os.environ.get("HB_REFERENCE", "/root/reference")
+    ref = os.environ.get("HB_REFERENCE")
+    if not ref or not (Path(ref) / "sa3jax").is_dir():
+        raise SystemExit("set HB_REFERENCE to a checkout of kelechi-c/hummingbird (the directory holding sa3jax/)")
     sys.path.insert(0, str(HERE / "_jaxshim"))
     sys.path.insert(0, ref)
     from sa3jax import config, dit, dtypes, same_l  # noqa: E402

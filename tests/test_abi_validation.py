@@ -78,6 +78,23 @@ def test_dense_noalloc_refuses_oversize_before_device_work(lib):
     assert lib.hb_dense_diff_attn_noalloc(*(_dense(batch=0)[:-3] + [None])) == _lib.HB_ERR_SHAPE
 
 
+def test_dense_noalloc_boundary_and_argument_checks_before_device_work(lib):
+    """The size limit is exact (a problem one row tile past 64 MiB is refused), and a problem that fits still has
+    its arguments checked on the host before the scratch is looked up on the device: a NULL or misaligned
+    pointer returns its own status with no GPU present."""
+    cap = 64 << 20
+    # one head pair: 10 prepared tiles per 128-row tile; 410 row tiles = 4,100 tiles > 4,096, 409 fit
+    over = _dense(length=410 * 128, heads=2, pair_count=1, qkv_rs=640, out_rs=128)[:-3] + [None]
+    assert _prep_bytes(1, 410 * 128, 2) > cap
+    assert lib.hb_dense_diff_attn_noalloc(*over) == _lib.HB_ERR_WORKSPACE
+    fits = dict(length=409 * 128, heads=2, pair_count=1, qkv_rs=640, out_rs=128)
+    assert _prep_bytes(1, 409 * 128, 2) <= cap
+    assert lib.hb_dense_diff_attn_noalloc(*(_dense(qkv=None, **fits)[:-3] + [None])) == _lib.HB_ERR_NULL
+    assert lib.hb_dense_diff_attn_noalloc(*(_dense(out=None, **fits)[:-3] + [None])) == _lib.HB_ERR_NULL
+    assert lib.hb_dense_diff_attn_noalloc(*(_dense(qkv=MIS, **fits)[:-3] + [None])) == _lib.HB_ERR_ALIGN
+    assert lib.hb_dense_diff_attn_noalloc(*(_dense(half=12, **fits)[:-3] + [None])) == _lib.HB_ERR_SHAPE
+
+
 def _band(**kw):
     """Arguments of a valid config-2 call (L = 82,688, 8 heads, window 128, partial RoPE), with overrides."""
     a = dict(qkv=P, qkv_rs=2560, q_norm=P, k_norm=P, inv_freq=P, half=16, lam=None, out=P, out_rs=512, batch=1,
