@@ -244,6 +244,50 @@ def time_band_e2e(step: BandStep, steps: int, warmup: int, world: int) -> dict:
     return {"ms_per_step": ms, "h2d": h_in.numel() * 2, "d2h": h_out.numel() * 2}
 
 
+def _gather_rows(vals: list, world: int) -> list:
+    """Every rank's list of floats, on every rank (rank order)."""
+    if world == 1:
+        return [vals]
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor(vals, dtype=torch.float64, device="cuda")
+    parts = [torch.empty_like(t) for _ in range(world)]
+    dist.all_gather(parts, t)
+    return [p.tolist() for p in parts]
+
+
+def band_parity(step: BandStep, world: int, edge: int = 384) -> dict:
+    """Output check of the headline step on every rank, outside the timed region: the first and the last `edge`
+    query rows this rank owns (at N > 1 these border the neighbouring shards, where the halo rows matter) against
+    the fp32 oracle (`oracle/band.py`) evaluated on the rank's buffer slice holding those rows and +-window keys,
+    at their global RoPE positions. Tolerance max-abs 2e-2, mean-abs 2e-3 (the north star's)."""
+    import torch
+    from hummingbird_b200._lib import HB_STAGE_ALL
+    from oracle import band as oband
+    step.exchange()
+    step.run(HB_STAGE_ALL)
+    torch.cuda.synchronize()
+    before, own, rows = step.before, L_PER_GPU, step.buf.shape[1]
+    w = step.w
+    worst, means = 0.0, []
+    for q0 in (0, own - edge):
+        s0 = max(0, before + q0 - WINDOW)
+        s1 = min(rows, before + q0 + edge + WINDOW)
+        qkv = step.buf[:, s0:s1].float().cpu().numpy()
+        ref = oband.band_diff_attention(qkv, w.q_norm, w.k_norm, w.inv_freq, HEADS, WINDOW, lam=w.lam,
+                                        offset=step.pos0 + s0)
+        a = before + q0 - s0
+        got = step.out[:, q0:q0 + edge].float().cpu().numpy()
+        diff = np.abs(got - ref[:, a:a + edge])
+        worst = max(worst, float(diff.max()))
+        means.append(float(diff.mean()))
+    mine = [worst, float(np.mean(means)), float(worst <= 2e-2 and np.mean(means) <= 2e-3)]
+    allr = _gather_rows(mine, world)
+    return {"ok": all(r[2] == 1.0 for r in allr), "max_abs": max(r[0] for r in allr),
+            "mean_abs": max(r[1] for r in allr), "per_rank": [[round(r[0], 5), round(r[1], 6)] for r in allr],
+            "rows": f"first and last {edge} own rows per rank vs the fp32 oracle"}
+
+
 # ----------------------------------------------------------------------------------------------- dense
 def _flush_l2(flush) -> None:
     """Evict L2 by reading a buffer twice its size: a read leaves the lines clean, so the timed call that follows
@@ -407,11 +451,10 @@ def _dit_clip_runner(model, shape, device, seed: int = 44):
     static = model.prepare_static(torch.randn(shape.batch, shape.context, shape.context_dim, generator=g, device=device),
                                   torch.randn(shape.batch, shape.context_dim, generator=g, device=device))
     sched = [float(v) for v in DiT.schedule(shape.steps, device=device)]
-    a, b = model.latent_range()
     x_full = torch.randn(shape.batch, shape.io_channels, shape.latents, generator=g, device=device).to(torch.bfloat16)
-    eps = torch.randn(shape.steps, shape.batch, shape.io_channels, shape.latents, generator=g,
-                      device=device).to(torch.bfloat16)[..., a:b].contiguous()
-    x0 = x_full[..., a:b].contiguous()
+    eps = model.local_view(torch.randn(shape.steps, shape.batch, shape.io_channels, shape.latents, generator=g,
+                                       device=device).to(torch.bfloat16))
+    x0 = model.local_view(x_full)
     x_in = x0.clone()
     t_cur = torch.zeros(shape.batch, device=device, dtype=torch.bfloat16)
     t_nxt = torch.zeros_like(t_cur)
@@ -441,8 +484,9 @@ def _dit_clip_runner(model, shape, device, seed: int = 44):
 
 def time_dit_clip(device, ff_quant: str, world: int = 1, clips: int = 3) -> dict:
     """Config 4: a whole 120 s clip (B=2 CFG pair, 2,584 latents + 64 memory tokens, 24 blocks, 8 pingpong
-    steps, random weights) through `hummingbird_b200.dit`, split over `world` GPUs (token rows + head pairs,
-    two NCCL all-to-alls per block) when world > 1. Returns ms per clip (max over ranks)."""
+    steps, random weights) through `hummingbird_b200.dit`, split over `world` GPUs when world > 1: the batch
+    rows over two rank groups, then token rows + head pairs inside a group (two NCCL all-to-alls per block).
+    Returns ms per clip (max over ranks)."""
     import torch
     import torch.distributed as dist
     from hummingbird_b200.config import DiTConfig
@@ -465,15 +509,50 @@ def time_dit_clip(device, ff_quant: str, world: int = 1, clips: int = 3) -> dict
     finite = bool(torch.isfinite(x.float()).all())
     del clip, held
     torch.cuda.synchronize()
-    return {"ms_per_clip": statistics.median(times), "n_gpus": world,
+    parity = dit_split_parity(model, shape, device, world, ff_quant) if world > 1 else None
+    return {"ms_per_clip": statistics.median(times), "n_gpus": world, "parity": parity,
             "config": "120 s clip: B=2 (CFG), 2,584 latents + 64 memory, 24 blocks, d 1024, 16 heads, 8 pingpong "
                       "steps, 128 context tokens, random weights",
             "mlp": "W8A8" if ff_quant == "w8a8" else "bf16 cuBLAS", "finite": finite,
             "glue": "fused row kernels (residual + RMSNorm + adaLN, GLU + quantise) and the fused "
                     "differential cross-attention kernel",
-            "parallelism": f"one clip over {world} GPUs: token rows x{world}, self-attention head pairs x{world}, "
-                           "2 NCCL all-to-alls per block" if world > 1 else "single GPU",
+            "parallelism": (f"one clip over {world} GPUs: the 2 batch rows over 2 groups of {world // 2} "
+                            "(no collective between them)" + (f"; inside each group token rows x{world // 2}, "
+                            f"self-attention head pairs x{world // 2}, 2 NCCL all-to-alls per block"
+                            if world > 2 else "")) if world > 1 else "single GPU",
             "how": "one denoise step captured in a CUDA graph, replayed 8 times per clip; CUDA events, max over ranks"}
+
+
+def dit_split_parity(model, shape, device, world: int, ff_quant: str) -> dict:
+    """The split clip's result checked outside the timed region: one denoise step of the model split over the
+    ranks (all ranks, gathered) against the same step of the unsplit model (same seed, so the same weights) on
+    rank 0 alone, on seeded inputs. Relative L2 difference < 2e-2 and max-abs reported (bf16 activations through
+    24 blocks; the two runs use different GEMM shapes, so they agree to rounding, not bit for bit)."""
+    import torch
+    import torch.distributed as dist
+    from hummingbird_b200.config import DiTConfig
+    from hummingbird_b200.dit import DiT
+    g = torch.Generator(device=device).manual_seed(77)
+    cross = torch.randn(shape.batch, shape.context, shape.context_dim, generator=g, device=device)
+    glob = torch.randn(shape.batch, shape.context_dim, generator=g, device=device)
+    x = torch.randn(shape.batch, shape.io_channels, shape.latents, generator=g, device=device).to(torch.bfloat16)
+    eps = torch.randn(shape.batch, shape.io_channels, shape.latents, generator=g, device=device).to(torch.bfloat16)
+    t = torch.full((shape.batch,), 0.9, device=device, dtype=torch.bfloat16)
+    tn = torch.full((shape.batch,), 0.5, device=device, dtype=torch.bfloat16)
+    got = model.gather_latents(model.step(model.local_view(x), t, tn, model.local_view(eps),
+                                          model.prepare_static(cross, glob))).float()
+    res = torch.zeros(3, dtype=torch.float64, device=device)
+    if dist.get_rank() == 0:
+        single = DiT(DiTConfig(ff_quant=ff_quant), shape, device)
+        expect = single.step(x, t, tn, eps, single.prepare_static(cross, glob)).float()
+        rel = ((got - expect).norm() / expect.norm()).item()
+        res[0], res[1] = rel, (got - expect).abs().max().item()
+        res[2] = float(bool(torch.isfinite(got).all()) and rel < 2e-2)
+        del single
+    dist.broadcast(res, 0)
+    torch.cuda.synchronize()
+    return {"ok": bool(res[2].item() == 1.0), "rel_l2": res[0].item(), "max_abs": res[1].item(),
+            "check": "one denoise step split over the ranks vs the unsplit model on one GPU"}
 
 
 SONG_LATENTS = 8184           # 380 s of audio
@@ -648,6 +727,33 @@ def run_reference(args, result_out):
     print(json.dumps(line), file=result_out, flush=True)
 
 
+def paths_summary(paths: dict, peaks: dict) -> dict:
+    """One short string per secondary path: time, rate and fraction of the measured peak."""
+    bf16 = peaks["bf16_tflops"]
+    out = {}
+    for key, name in (("dense_config1", "dense_c1"), ("dense_120s_block_call", "dense_120s_block")):
+        if key in paths:
+            d = paths[key]
+            out[name] = f"{d['ms']:.4f} ms {d['tflops']:.0f} TFLOP/s {d['tflops'] / bf16:.1%} bf16"
+    if "cross_120s_block_call" in paths:
+        d = paths["cross_120s_block_call"]
+        out["cross_120s_block"] = f"{d['ms']:.4f} ms {d['gbs']:.0f} GB/s {d['hbm_frac']:.1%} HBM"
+    if "w8a8_config3" in paths:
+        d = paths["w8a8_config3"]
+        pk = d["int8_peak_tops_measured"]
+        out["w8a8_c3"] = (f"g1 {d['gemm1_ms'] * 1e3:.1f} us {d['gemm1_tops']:.0f} TOPS {d['gemm1_tops'] / pk:.0%}; "
+                          f"g2 {d['gemm2_ms'] * 1e3:.1f} us {d['gemm2_tops']:.0f} TOPS {d['gemm2_tops'] / pk:.0%}")
+    for key, name in (("dit_120s_clip_bf16_mlp", "dit_120s_bf16"), ("dit_120s_clip_w8a8_mlp", "dit_120s_w8a8")):
+        if key in paths:
+            out[name] = f"{paths[key]['ms_per_clip']:.1f} ms/clip"
+    if "band_380s_layer" in paths:
+        d = paths["band_380s_layer"]
+        out["band_380s"] = f"{d['ms_per_layer']:.3f} ms {d['tflops']:.0f} TFLOP/s"
+    if "song_380s_8_clips" in paths:
+        out["song_380s_x8"] = f"{paths['song_380s_8_clips']['ms_per_batch_of_8']:.0f} ms"
+    return out
+
+
 # ----------------------------------------------------------------------------------------------- main
 def _stdout_for_result():
     """Route everything written to fd 1 (library banners, NCCL) to stderr; return a stream on the original
@@ -741,6 +847,12 @@ def main():
         line["cpu_baseline"] = cpu_band_baseline(step.w.qkv, step.w, args.cpu_rows)
         from oracle.cpu_baseline import shutdown
         shutdown()
+    parity = {"band_headline": band_parity(step, world)}
+    if "paths" in line and line["paths"]["dit_120s_clip_w8a8_mlp"].get("parity"):
+        parity["dit_split_step"] = line["paths"]["dit_120s_clip_w8a8_mlp"]["parity"]
+    line["parity"] = parity
+    if "paths" in line:  # the secondary paths in one short entry, last on the line
+        line["paths_summary"] = paths_summary(line["paths"], peaks)
     if rank == 0:
         print(json.dumps(line), file=result_out, flush=True)
     if world > 1:

@@ -9,9 +9,13 @@ residual / RMSNorm / adaLN / GLU steps its row kernels; projections are torch ma
 `glue="torch"` the cross-attention and the elementwise steps run as torch ops (cuDNN-flash SDPA). No checkpoint
 is loaded: weights are N(0, 1 / fan_in) bf16 draws.
 
-With a process group of N ranks (one per GPU) one clip runs on all N: token-wise work is split by token rows
-and the self-attention by head pairs, with two all-to-alls per block (`hummingbird_b200.parallel`); each rank
-holds the latents of its token rows (`latent_range`) and `gather_latents` rebuilds the whole clip.
+With a process group of N ranks (one per GPU) one clip runs on all N. The clip's batch rows are independent
+through the whole denoise (the reference runs its CFG pair as a plain batch: guidance is off at
+`cfg_scale=1.0`, dit.py:11), so they are split first: with B=2 and N even, ranks [0, N/2) take row 0 and
+[N/2, N) row 1, with no collective between the halves. Inside each half of more than one rank, token-wise work
+is split by token rows and the self-attention by head pairs, with two all-to-alls per block
+(`hummingbird_b200.parallel`). Each rank holds its batch rows (`batch_range`) of the latents of its token rows
+(`latent_range`); `local_view` cuts a whole-clip tensor to that part and `gather_latents` rebuilds the clip.
 
 Cast points follow the reference under the BF16 preset: bf16 activations, RMSNorm in fp32 cast back
 (dit.py:45-57), the adaLN gate `sigmoid(1 - gate)` (dit.py:227), cross K/V hoisted once per clip and k-normed
@@ -20,7 +24,7 @@ Cast points follow the reference under the BF16 preset: bf16 activations, RMSNor
 from __future__ import annotations
 
 import math
-from dataclasses import dataclass
+from dataclasses import dataclass, replace
 
 import torch
 import torch.distributed as dist
@@ -73,15 +77,32 @@ class DiT:
     kernels (`hummingbird_b200.dit_glue`); "torch" runs them as separate torch ops (the reference's op order)."""
 
     def __init__(self, cfg: DiTConfig, shape: ClipShape, device, seed: int = 4, *, group=None, attend=None,
-                 glue: str = "cuda"):
-        self.cfg, self.shape, self.device = cfg, shape, device
+                 glue: str = "cuda", split_batch: bool = True):
+        self.cfg, self.full_shape, self.device = cfg, shape, device
         self.attend = attend or hb_dense.dense_attention
         if glue not in ("cuda", "torch"):
             raise ValueError(f"glue must be 'cuda' or 'torch', not {glue!r}")
         self.glue = glue
+        # batch rows over groups of ranks first (independent rows, no collective between the groups), then
+        # token rows / head pairs inside each group
+        self.outer = group
+        world_all = dist.get_world_size(group) if group is not None else 1
+        rank_all = dist.get_rank(group) if group is not None else 0
+        nb = math.gcd(shape.batch, world_all) if split_batch and world_all > 1 else 1
+        inner = world_all // nb
+        bg = rank_all // inner
+        self.batch_groups = nb
+        self.batch_range = (shape.batch * bg // nb, shape.batch * (bg + 1) // nb)
+        if nb > 1:
+            shape = replace(shape, batch=shape.batch // nb)
+            # every rank creates every subgroup, in the same order (torch.distributed.new_group is collective)
+            subgroups = [dist.new_group(list(range(k * inner, (k + 1) * inner))) if inner > 1 else None
+                         for k in range(nb)]
+            group = subgroups[bg]
+        self.shape = shape
         self.group = group
-        self.world = dist.get_world_size(group) if group is not None else 1
-        self.rank = dist.get_rank(group) if group is not None else 0
+        self.world = inner if nb > 1 else world_all
+        self.rank = rank_all - bg * inner if nb > 1 else rank_all
         self.seq = cfg.num_memory_tokens + shape.latents
         self.t0, self.t1 = par.shard_tokens(self.seq, self.world, self.rank)
         self.mem_rows = max(0, min(self.t1, cfg.num_memory_tokens) - self.t0)
@@ -136,7 +157,9 @@ class DiT:
 
     # ------------------------------------------------------------------ per clip
     def prepare_static(self, cross_cond: torch.Tensor, global_cond: torch.Tensor) -> dict:
-        """`dit.prepare_static` (dit.py:287-337): hoisted, k-normed cross K/V per block, conditioning, tables."""
+        """`dit.prepare_static` (dit.py:287-337): hoisted, k-normed cross K/V per block, conditioning, tables.
+        The conditioning may hold the whole clip's batch rows; this rank's are taken."""
+        cross_cond, global_cond = self._rows(cross_cond), self._rows(global_cond)
         cfg, d, h = self.cfg, self.cfg.embed_dim, self.cfg.num_heads
         seq = cfg.num_memory_tokens + self.shape.latents
         valid = torch.ones(self.shape.batch, seq, device=self.device)
@@ -165,24 +188,43 @@ class DiT:
         mem = self.cfg.num_memory_tokens
         return max(self.t0, mem) - mem, self.t1 - mem
 
+    def _rows(self, t: torch.Tensor) -> torch.Tensor:
+        """This rank's batch rows of a tensor that holds the whole clip's batch (others pass through)."""
+        if self.batch_groups > 1 and t.shape[0] == self.full_shape.batch:
+            return t[self.batch_range[0]:self.batch_range[1]]
+        return t
+
+    def local_view(self, x: torch.Tensor) -> torch.Tensor:
+        """The whole clip's `(..., B, io, T)` latents -> this rank's `(..., B_r, io, T_r)` part (contiguous)."""
+        a, b = self.latent_range()
+        b0, b1 = self.batch_range
+        return x[..., b0:b1, :, a:b].contiguous()
+
     def gather_latents(self, x_local: torch.Tensor) -> torch.Tensor:
-        """All ranks' `(B, io, T_r)` latent slices -> the whole clip `(B, io, T)`."""
-        if self.world == 1:
-            return x_local
-        mem = self.cfg.num_memory_tokens
-        spans = [par.shard_tokens(self.seq, self.world, r) for r in range(self.world)]
-        widths = [t1 - max(t0, mem) for t0, t1 in spans]
-        padded = x_local.new_zeros(*x_local.shape[:2], max(widths))
-        padded[..., :x_local.shape[-1]] = x_local
-        parts = [torch.empty_like(padded) for _ in range(self.world)]
-        dist.all_gather(parts, padded, group=self.group)
-        return torch.cat([part[..., :w] for part, w in zip(parts, widths)], -1)
+        """All ranks' `(B_r, io, T_r)` parts -> the whole clip `(B, io, T)`."""
+        x = x_local
+        if self.world > 1:
+            mem = self.cfg.num_memory_tokens
+            spans = [par.shard_tokens(self.seq, self.world, r) for r in range(self.world)]
+            widths = [t1 - max(t0, mem) for t0, t1 in spans]
+            padded = x.new_zeros(*x.shape[:2], max(widths))
+            padded[..., :x.shape[-1]] = x
+            parts = [torch.empty_like(padded) for _ in range(self.world)]
+            dist.all_gather(parts, padded, group=self.group)
+            x = torch.cat([part[..., :w] for part, w in zip(parts, widths)], -1)
+        if self.batch_groups > 1:  # one copy of each batch group's rows (every rank of a group holds them)
+            parts = [torch.empty_like(x) for _ in range(dist.get_world_size(self.outer))]
+            dist.all_gather(parts, x.contiguous(), group=self.outer)
+            inner = len(parts) // self.batch_groups
+            x = torch.cat([parts[k * inner] for k in range(self.batch_groups)], 0)
+        return x
 
     # ------------------------------------------------------------------ denoiser
     def forward(self, x: torch.Tensor, t: torch.Tensor, static: dict) -> torch.Tensor:
         """`dit_forward`: `(B, io, T_r)` latents (this rank's `latent_range`; all T on one GPU) and `(B,)`
         timesteps -> velocity of the same shape (dit.py:340-361)."""
         cfg, p = self.cfg, self.p
+        t = self._rows(t)
         h = x.to(torch.bfloat16)
         h = torch.einsum("bct,oc->bot", h, p["preprocess_conv"]) + h
         h = h.transpose(1, 2) @ p["project_in"].T
@@ -306,6 +348,7 @@ class DiT:
 
     def step(self, x, t_curr, t_next, eps, static):
         """One pingpong step (sampling.py:109-113)."""
+        t_curr, t_next = self._rows(t_curr), self._rows(t_next)
         v = self.forward(x, t_curr, static)
         denoised = x - t_curr[:, None, None] * v
         return (1 - t_next[:, None, None]) * denoised + t_next[:, None, None] * eps

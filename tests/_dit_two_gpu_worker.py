@@ -28,9 +28,9 @@ def main():
     tn = torch.full((2,), 0.5, device="cuda", dtype=torch.bfloat16)
     single = DiT(cfg, shape, "cuda")
     expect = single.step(x, t, tn, eps, single.prepare_static(cross, glob)).float()
-    model = DiT(cfg, shape, "cuda", group=dist.group.WORLD)
-    a, b = model.latent_range()
-    got = model.gather_latents(model.step(x[..., a:b].contiguous(), t, tn, eps[..., a:b].contiguous(),
+    split = os.environ.get("HB_DIT_SPLIT_BATCH", "1") == "1"
+    model = DiT(cfg, shape, "cuda", group=dist.group.WORLD, split_batch=split)
+    got = model.gather_latents(model.step(model.local_view(x), t, tn, model.local_view(eps),
                                           model.prepare_static(cross, glob))).float()
     rel = ((got - expect).norm() / expect.norm()).item()
     ok = got.shape == expect.shape and bool(torch.isfinite(got).all()) and rel < 2e-2

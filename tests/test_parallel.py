@@ -106,12 +106,13 @@ def _stand_in_attention(qkv, q_w, k_w, cos, sin, mask, num_heads, head_dim, half
     return out.permute(0, 2, 1, 3).reshape(b, length, num_heads * head_dim).bfloat16()
 
 
-def _tiny_dit(group):
+def _tiny_dit(group, split_batch=True):
     from hummingbird_b200.config import DiTConfig
     from hummingbird_b200.dit import ClipShape, DiT
     cfg = DiTConfig(embed_dim=512, num_heads=8, num_memory_tokens=8)
     shape = ClipShape(batch=2, latents=88, io_channels=16, context=8, context_dim=32, depth=2, steps=2)
-    return DiT(cfg, shape, "cpu", group=group, attend=_stand_in_attention, glue="torch"), shape
+    return DiT(cfg, shape, "cpu", group=group, attend=_stand_in_attention, glue="torch",
+               split_batch=split_batch), shape
 
 
 def _dit_inputs(shape):
@@ -122,23 +123,27 @@ def _dit_inputs(shape):
     return cross, glob, x
 
 
-def _dit_worker(rank, world):
+def _dit_worker(rank, world, split_batch):
     full, shape = _tiny_dit(None)
     cross, glob, x = _dit_inputs(shape)
-    t = torch.full((shape.batch,), 0.7).bfloat16()
+    t = torch.tensor([0.7, 0.4]).bfloat16()  # a different timestep per batch row: the rows must not mix
     expect = full.forward(x, t, full.prepare_static(cross, glob)).float()
-    model, _ = _tiny_dit(dist.group.WORLD)
-    a, b = model.latent_range()
-    got = model.gather_latents(model.forward(x[..., a:b], t, model.prepare_static(cross, glob))).float()
+    model, _ = _tiny_dit(dist.group.WORLD, split_batch)
+    got = model.gather_latents(model.forward(model.local_view(x), t, model.prepare_static(cross, glob))).float()
     assert got.shape == expect.shape
     rel = ((got - expect).norm() / expect.norm()).item()
     assert rel < 1e-2, f"rank {rank}: sharded DiT differs from the single-rank one (relative {rel:.2e})"
+    if split_batch and world == 2:  # one batch row per rank, nothing split inside it: the same bits
+        assert model.world == 1 and model.batch_range == (rank, rank + 1)
+        assert torch.equal(got, expect)
 
 
-@pytest.mark.parametrize("world", [2, 4])
-def test_dit_token_and_pair_sharding_gloo(world):
-    """One clip over 2 / 4 ranks (token rows + head pairs, two all-to-alls per block) equals one rank."""
-    _run(_dit_worker, world)
+@pytest.mark.parametrize("world,split_batch", [(2, True), (4, True), (2, False), (4, False)])
+def test_dit_sharding_gloo(world, split_batch):
+    """One clip over 2 / 4 ranks equals one rank: batch rows over rank groups (no collective between them), then
+    token rows + head pairs inside each group (two all-to-alls per block); or token rows + head pairs over all
+    ranks when the batch is not split."""
+    _run(_dit_worker, world, split_batch)
 
 
 def test_dit_sharding_rejects_uneven_pairs():
