@@ -9,5 +9,9 @@ def softmax(x, axis=-1):
     return unnormalized / _np.sum(unnormalized.astype(_np.float64), axis=axis, keepdims=True).astype(x.dtype)
 
 
+def sigmoid(x):
+    return 1.0 / (1.0 + _np.exp(-x))
+
+
 def silu(x):
     return x / (1.0 + _np.exp(-x))

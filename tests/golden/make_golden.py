@@ -16,6 +16,8 @@ reference checkout named by `$HB_REFERENCE` (required). The reference then runs 
   (dit.py:274-284), identity `to_q` / `to_kv` / `to_out`; branches A and B with `differential=False`.
 * w8a8: no reference exists; the accumulators come from a pure-Python integer dot product, independent
   of the numpy oracle.
+* dit block: `sa3jax.dit._block` (dit.py:224-250) on one block with random weights, cross K/V from
+  `sa3jax.dit._cross_kv` (dit.py:274-284).
 
 Run from the repo root:  HB_REFERENCE=<path of a hummingbird checkout> python tests/golden/make_golden.py
 This script (and only this script) reads the reference; the fixtures it writes are what tests use.
@@ -162,6 +164,64 @@ def band_case(name, *, seed, batch, length, heads, half, window, alpha=0.5, gamm
     print(f"{name}: out absmax {np.abs(out).max():.4f}")
 
 
+def dit_block_case(name, *, seed, batch, latents, memory, context, heads):
+    """`sa3jax.dit._block` (dit.py:224-250): one whole block (adaLN, self-attention, gated residuals, cross-attention
+    over K/V hoisted by `sa3jax.dit._cross_kv`, `to_local_embed` on the non-memory rows, GLU MLP) with random,
+    bf16-representable weights, `attention="xla"`, `differential=True`, under `FP32_PARITY`."""
+    config, dit, dtypes, _ = _import_reference()
+    rng = np.random.default_rng(seed)
+    d = heads * 64
+    cfg = config.DiTConfig(embed_dim=d, num_heads=heads, differential=True, attention="xla",
+                           num_memory_tokens=memory)
+    inner = cfg.ff_inner
+    length = memory + latents
+
+    def w(*shape, fan_in=None, scale=1.0):
+        fan = fan_in or shape[-1]
+        return _bf16(scale * rng.standard_normal(shape) / np.sqrt(fan))[1]
+
+    def near_one(n):
+        return _bf16(1.0 + 0.1 * rng.standard_normal(n))[1]
+
+    p = {"to_scale_shift_gate": _bf16(0.3 * rng.standard_normal(6 * d))[1],
+         "pre_norm": near_one(d), "cross_attend_norm": near_one(d), "ff_norm": near_one(d),
+         "sa_to_qkv": w(5 * d, d), "sa_q_norm": near_one(64), "sa_k_norm": near_one(64), "sa_to_out": w(d, d),
+         "ca_to_q": w(2 * d, d), "ca_to_kv": w(3 * d, d), "ca_q_norm": near_one(64), "ca_k_norm": near_one(64),
+         "ca_to_out": w(d, d), "local": _bf16(0.2 * rng.standard_normal(d))[1],
+         "glu_w": w(2 * inner, d), "glu_b": _bf16(0.05 * rng.standard_normal(2 * inner))[1],
+         "proj_w": w(d, inner), "proj_b": _bf16(0.05 * rng.standard_normal(d))[1]}
+    h_bits, h = _bf16(rng.standard_normal((batch, length, d)))
+    ctx_bits, ctx = _bf16(rng.standard_normal((batch, context, d)))
+    gcond_bits, gcond = _bf16(0.3 * rng.standard_normal((batch, 6 * d)))
+    freqs = _inv_freq(cfg.rope_dim // 2)
+    f32 = dtypes.FP32_PARITY
+    block = {"to_scale_shift_gate": p["to_scale_shift_gate"],
+             "pre_norm": {"weight": p["pre_norm"]}, "cross_attend_norm": {"weight": p["cross_attend_norm"]},
+             "ff_norm": {"weight": p["ff_norm"]},
+             "self_attn": {"to_qkv": {"weight": p["sa_to_qkv"]}, "q_norm": {"weight": p["sa_q_norm"]},
+                           "k_norm": {"weight": p["sa_k_norm"]}, "to_out": {"weight": p["sa_to_out"]}},
+             "cross_attn": {"to_q": {"weight": p["ca_to_q"]}, "to_kv": {"weight": p["ca_to_kv"]},
+                            "q_norm": {"weight": p["ca_q_norm"]}, "k_norm": {"weight": p["ca_k_norm"]},
+                            "to_out": {"weight": p["ca_to_out"]}},
+             "ff": {"glu_proj": {"weight": p["glu_w"], "bias": p["glu_b"]},
+                    "proj_out": {"weight": p["proj_w"], "bias": p["proj_b"]}}}
+    k, kd, v = dit._cross_kv(block, ctx.astype(np.float32), cfg, f32)
+    cos, sin = dit._rope_tables(length, freqs)
+    valid = np.ones((batch, length), np.float32)
+    static = {"cos": cos, "sin": sin, "v_mask": valid[:, None, :, None], "cross_k": [k], "cross_v": [v],
+              "cross_k_diff": [kd], "local": [p["local"]]}
+    import jax.numpy as jnp  # the numpy stand-in, on sys.path after _import_reference()
+    out = dit._block(jnp.array_at(h.astype(np.float32)), block, static, gcond.astype(np.float32), 0, cfg, f32)
+    out = np.asarray(out)
+    merge = lambda t: np.asarray(t).transpose(0, 2, 1, 3).reshape(batch, context, d)  # noqa: E731
+    kv_normed = np.concatenate([merge(k), merge(kd), merge(v)], -1).astype(np.float32)
+    np.savez_compressed(HERE / f"{name}.npz", h_bits=h_bits, ctx_bits=ctx_bits, gcond_bits=gcond_bits,
+                        inv_freq=freqs, heads=heads, memory=memory, norm_eps=np.float32(cfg.norm_eps),
+                        qk_eps=np.float32(cfg.qk_norm_eps), kv_normed=kv_normed, out_ref=out.astype(np.float32),
+                        **{f"p_{key}": _bf16(val)[0] for key, val in p.items()})  # bf16 bit patterns
+    print(f"{name}: out absmax {np.abs(out).max():.4f}")
+
+
 def w8a8_case(name, *, seed, m, k, n):
     """Integer accumulators by a pure-Python dot product (independent of numpy's int matmul)."""
     sys.path.insert(0, str(ROOT))
@@ -197,6 +257,7 @@ def main():
     band_case("band_w17_l136_sharp", seed=22, batch=1, length=136, heads=2, half=16, window=17, alpha=1.5,
               gamma=4.0)
     w8a8_case("w8a8_m9_k96_n12", seed=30, m=9, k=96, n=12)
+    dit_block_case("dit_block_d256_l136", seed=50, batch=2, latents=128, memory=8, context=16, heads=4)
 
 
 if __name__ == "__main__":

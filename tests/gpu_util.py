@@ -38,3 +38,15 @@ def fp32_tolerance(fused_ref: np.ndarray, fp32_ref: np.ndarray) -> tuple[float, 
     (large only for the deliberately sharp fixtures, where bf16 q/k operands move near-argmax weights)."""
     d = np.abs(fused_ref.astype(np.float64) - fp32_ref)
     return max(2e-2, 1.25 * float(d.max())), max(2e-3, 1.25 * float(d.mean()))
+
+
+# The composed DiT block (bf16 activations, bf16 / W8A8 GEMMs) against the fp32 reference `_block`: relative L2
+# error per row group (the memory-token rows and the latent rows separately).
+BLOCK_REL_TOL = 1.5e-2
+
+
+def block_rel_errors(out: np.ndarray, ref: np.ndarray, memory: int) -> tuple[float, float]:
+    """Relative L2 difference on the memory rows and on the latent rows of a `(B, L, d)` block output."""
+    out, ref = np.asarray(out, np.float64), np.asarray(ref, np.float64)
+    rel = lambda a, b: float(np.linalg.norm(a - b) / np.linalg.norm(b))  # noqa: E731
+    return rel(out[:, :memory], ref[:, :memory]), rel(out[:, memory:], ref[:, memory:])

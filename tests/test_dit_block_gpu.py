@@ -1,0 +1,86 @@
+"""GPU: one composed DiT block of `hummingbird_b200.dit` against the reference's own `dit._block` (dit.py:224-250).
+
+The golden fixture `dit_block_d256_l136` holds the reference's fp32 output for one block with random weights
+(d 256, 4 heads, 8 memory tokens + 128 latents, B=2, 16 context tokens); `oracle.dit_block` restates it and is
+pinned to it on the CPU. Here the same weights drive this library's block: with the fused row kernels
+(residual + RMSNorm + adaLN, GLU + quantise, the cross-attention kernel) and with torch glue, each with the bf16
+and the W8A8 MLP. The self-attention is the fused dense kernel in every case. Tolerance: relative L2 error per
+row group (memory rows, latent rows) below `BLOCK_REL_TOL`, for bf16 activations against fp32.
+"""
+import numpy as np
+import pytest
+import torch
+
+from conftest import load_golden
+from gpu_util import BLOCK_REL_TOL, bf16_cuda, block_rel_errors, to_np
+
+pytestmark = pytest.mark.gpu
+
+
+def _model_with_golden_block(z, ff_quant: str, glue: str):
+    from hummingbird_b200.config import DiTConfig
+    from hummingbird_b200.dit import ClipShape, DiT
+    from hummingbird_b200.w8a8 import W8A8Linear
+    heads, memory = int(z["heads"]), int(z["memory"])
+    batch, length, d = z["h_bits"].shape
+    cfg = DiTConfig(embed_dim=d, num_heads=heads, num_memory_tokens=memory, ff_quant=ff_quant,
+                    norm_eps=float(z["norm_eps"]), qk_norm_eps=float(z["qk_eps"]))
+    shape = ClipShape(batch=batch, latents=length - memory, io_channels=16, context=z["ctx_bits"].shape[1],
+                      context_dim=32, depth=1, steps=1)
+    model = DiT(cfg, shape, "cuda", glue=glue)
+    w = {k[2:]: bf16_cuda(v) for k, v in z.items() if k.startswith("p_")}
+    b = model.blocks[0]
+    b["to_scale_shift_gate"] = w["to_scale_shift_gate"]
+    for name in ("pre_norm", "cross_attend_norm", "ff_norm"):
+        b[name] = w[name].float()
+        b[name + "_bf"] = w[name]
+    b["self_attn"].update(to_qkv=w["sa_to_qkv"], to_out=w["sa_to_out"], q_norm=w["sa_q_norm"].float(),
+                          k_norm=w["sa_k_norm"].float())
+    b["cross_attn"].update(to_q=w["ca_to_q"], to_kv=w["ca_to_kv"], to_out=w["ca_to_out"],
+                           q_norm=w["ca_q_norm"].float(), q_norm_bf=w["ca_q_norm"], q_norm_f=w["ca_q_norm"].float(),
+                           k_norm=w["ca_k_norm"].float())
+    b["local"] = w["local"]
+    b["glu"] = {"w": w["glu_w"], "b": w["glu_b"]}
+    b["proj_out"] = {"w": w["proj_w"], "b": w["proj_b"]}
+    if ff_quant == "w8a8":
+        b["glu_q"] = W8A8Linear(w["glu_w"], w["glu_b"])
+        b["proj_out_q"] = W8A8Linear(w["proj_w"], w["proj_b"])
+    model.p["rope_inv_freq"] = torch.from_numpy(z["inv_freq"]).cuda()
+    return model, b
+
+
+def _static(model, z):
+    """The block's per-clip tensors: lane RoPE tables, and the reference's hoisted k-normed cross K/V in both
+    layouts (rows for the cross-attention kernel, per-head tensors for the torch glue)."""
+    from hummingbird_b200 import dense_attention as hb_dense
+    batch, length, d = z["h_bits"].shape
+    heads = int(z["heads"])
+    valid = torch.ones(batch, length, device="cuda")
+    cos, sin, mask = hb_dense.tables(length, model.p["rope_inv_freq"], valid, 64)
+    kv = torch.from_numpy(z["kv_normed"]).cuda().to(torch.bfloat16)  # (B, C, [k | k_diff | v])
+    k, kd, v = (t.unflatten(-1, (heads, 64)).transpose(1, 2) for t in kv.chunk(3, -1))
+    return {"lane_cos": cos, "lane_sin": sin, "lane_mask": mask, "cross_kv_rows": [kv.contiguous()],
+            "cross_kv": [(k, kd, v)]}
+
+
+@pytest.mark.parametrize("glue", ["cuda", "torch"])
+@pytest.mark.parametrize("ff_quant", ["none", "w8a8"])
+def test_dit_block_matches_reference_block(cuda_lib, glue, ff_quant):
+    from hummingbird_b200 import _lib
+    z = load_golden("dit_block_d256_l136")
+    model, b = _model_with_golden_block(z, ff_quant, glue)
+    static = _static(model, z)
+    h = bf16_cuda(z["h_bits"])
+    gcond = bf16_cuda(z["gcond_bits"])
+    with torch.no_grad():
+        if glue == "cuda":
+            out = model._blocks_fused(h.clone(), static, gcond)  # one block (depth 1); updates its h in place
+        else:
+            out = model._block(h, b, static, gcond, 0)
+    torch.cuda.synchronize()
+    got = to_np(out)
+    assert np.all(np.isfinite(got))
+    rel_mem, rel_lat = block_rel_errors(got, z["out_ref"], int(z["memory"]))
+    print(f"{glue} glue, {ff_quant} MLP: relative L2 memory rows {rel_mem:.2e}, latent rows {rel_lat:.2e}")
+    assert rel_mem < BLOCK_REL_TOL and rel_lat < BLOCK_REL_TOL, (rel_mem, rel_lat)
+    assert _lib.device_status() == 0

@@ -127,3 +127,43 @@ def test_quantize_rounding_rules():
     assert s[0] == 1.0 and s[1] == 1.0
     assert q[0].tolist() == [127, 2, -4, 0, 0, 2, 126, -127]
     assert q[1].tolist() == [0] * 8
+
+
+def _block_args(z):
+    p = {k[2:]: bf16_bits_to_f32(v) for k, v in z.items() if k.startswith("p_")}
+    h = bf16_bits_to_f32(z["h_bits"])
+    valid = np.ones(h.shape[:2], np.float32)
+    return (h, p, bf16_bits_to_f32(z["gcond_bits"]), z["kv_normed"], z["inv_freq"], valid), \
+        dict(num_heads=int(z["heads"]), memory=int(z["memory"]), norm_eps=float(z["norm_eps"]),
+             qk_eps=float(z["qk_eps"]))
+
+
+def test_dit_block_oracle_matches_reference():
+    """`oracle.dit_block` against the reference's own `dit._block` (dit.py:224-250) on random weights."""
+    from oracle.dit_block import dit_block
+    z = load_golden("dit_block_d256_l136")
+    args, kw = _block_args(z)
+    out = dit_block(*args, **kw)
+    check_close(out, z["out_ref"], max_abs=1e-4, mean_abs=1e-5)
+
+
+@pytest.mark.parametrize("mistake", ["gate_without_one_minus", "local_on_memory_rows", "no_adaln_shift"])
+def test_dit_block_fixture_catches_order_mistakes(mistake, monkeypatch):
+    """Each of these slips in the block's composition moves the output, on the memory rows or on the latent rows,
+    by more than 3x the bf16 tolerance the GPU test of the composed block uses per row group, so that test would
+    catch it. The mistakes are planted in the oracle, on the CPU."""
+    from gpu_util import BLOCK_REL_TOL, block_rel_errors
+    from oracle import dit_block as ob
+    z = load_golden("dit_block_d256_l136")
+    args, kw = _block_args(z)
+    h, p, gcond, kv, freqs, valid = args
+    if mistake == "gate_without_one_minus":
+        monkeypatch.setattr(ob, "_sigmoid", lambda x: 1.0 / (1.0 + np.exp(x - 1.0)))  # sigmoid(gate), not of 1 - gate
+    elif mistake == "local_on_memory_rows":
+        kw = dict(kw, memory=0)
+    else:
+        gcond = gcond.copy()
+        gcond[:, 256:512] = -p["to_scale_shift_gate"][256:512]  # cancels shift_self: x * (1 + scale) only
+    out = ob.dit_block(h, p, gcond, kv, freqs, valid, **kw)
+    worst = max(block_rel_errors(out, z["out_ref"], int(z["memory"])))
+    assert worst > 3 * BLOCK_REL_TOL, f"{mistake}: relative change {worst:.3e} too small to be caught"
