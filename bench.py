@@ -441,45 +441,26 @@ def time_w8a8(device, steps: int, warmup: int) -> dict:
 
 # ----------------------------------------------------------------------------------------------- DiT clip
 def _dit_clip_runner(model, shape, device, seed: int = 44):
-    """Inputs of one clip and a `clip()` that denoises it: one denoise step captured in a CUDA graph (NCCL
-    all-to-alls included when the clip is split over ranks), replayed `shape.steps` times. Returns `clip` and
-    the objects the graph reads (the graph itself, the per-clip static tensors): the caller keeps them alive
-    while it replays and releases them together."""
+    """Inputs of one clip and a `clip()` that denoises it: the whole 8-step denoise loop captured in one CUDA graph
+    (`DiT.denoise_graph`; NCCL all-to-alls included when the clip is split over ranks inside a batch group),
+    replayed once per clip. Returns `clip` and the objects the graph reads (the graph itself, the per-clip static
+    tensors): the caller keeps them alive while it replays and releases them together."""
     import torch
-    from hummingbird_b200.dit import DiT
     g = torch.Generator(device=device).manual_seed(seed)
     static = model.prepare_static(torch.randn(shape.batch, shape.context, shape.context_dim, generator=g, device=device),
                                   torch.randn(shape.batch, shape.context_dim, generator=g, device=device))
-    sched = [float(v) for v in DiT.schedule(shape.steps, device=device)]
     x_full = torch.randn(shape.batch, shape.io_channels, shape.latents, generator=g, device=device).to(torch.bfloat16)
     eps = model.local_view(torch.randn(shape.steps, shape.batch, shape.io_channels, shape.latents, generator=g,
                                        device=device).to(torch.bfloat16))
     x0 = model.local_view(x_full)
     x_in = x0.clone()
-    t_cur = torch.zeros(shape.batch, device=device, dtype=torch.bfloat16)
-    t_nxt = torch.zeros_like(t_cur)
-    e_in = torch.empty_like(x_in)
-    side = torch.cuda.Stream(device)
-    side.wait_stream(torch.cuda.current_stream(device))
-    with torch.cuda.stream(side):
-        for _ in range(2):
-            model.step(x_in, t_cur, t_nxt, e_in, static)
-    torch.cuda.current_stream(device).wait_stream(side)
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph):
-        x_out = model.step(x_in, t_cur, t_nxt, e_in, static)
+    run, graph = model.denoise_graph(x_in, eps, static, shape.steps)
 
     def clip():
         x_in.copy_(x0)
-        for s in range(shape.steps):
-            t_cur.fill_(sched[s])
-            t_nxt.fill_(sched[s + 1])
-            e_in.copy_(eps[s])
-            graph.replay()
-            x_in.copy_(x_out)
-        return x_in
+        return run()
 
-    return clip, (graph, static)
+    return clip, (graph, static, eps, x_in)
 
 
 def time_dit_clip(device, ff_quant: str, world: int = 1, clips: int = 3) -> dict:
@@ -520,7 +501,8 @@ def time_dit_clip(device, ff_quant: str, world: int = 1, clips: int = 3) -> dict
                             "(no collective between them)" + (f"; inside each group token rows x{world // 2}, "
                             f"self-attention head pairs x{world // 2}, 2 NCCL all-to-alls per block"
                             if world > 2 else "")) if world > 1 else "single GPU",
-            "how": "one denoise step captured in a CUDA graph, replayed 8 times per clip; CUDA events, max over ranks"}
+            "how": "the whole 8-step denoise loop captured in one CUDA graph, one replay per clip; CUDA events, max "
+                   "over ranks"}
 
 
 def dit_split_parity(model, shape, device, world: int, ff_quant: str) -> dict:

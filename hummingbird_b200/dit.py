@@ -346,6 +346,40 @@ class DiT:
         out[0] = sigma_max
         return out
 
+    def denoise_graph(self, x0: torch.Tensor, eps: torch.Tensor, static: dict, steps: int | None = None):
+        """`sampling.pingpong` (sampling.py:81-118, one `lax.scan` over the steps) as one CUDA graph: every step
+        of the denoise loop, the schedule's timesteps baked in as constants, replayed with one launch per clip.
+
+        `x0` is this rank's `(B_r, io, T_r)` initial latents and `eps` its `(steps, B_r, io, T_r)` noise, both
+        read by the graph (refill `x0` in place between replays). Returns `run`, which replays the graph and
+        returns the final latents (a tensor the graph owns, overwritten by the next replay), and the graph:
+        keep it alive while replaying, and release it before the process group when the loop holds
+        collectives. Capture needs a CUDA device."""
+        steps = self.shape.steps if steps is None else steps
+        sched = [float(v) for v in self.schedule(steps, device=x0.device)]
+        bsz, dev = x0.shape[0], x0.device
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):  # warm-up outside the capture: library handles and workspaces
+            t = torch.full((bsz,), sched[0], device=dev, dtype=torch.bfloat16)
+            for _ in range(2):
+                self.step(x0, t, t, eps[0], static)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            x = x0
+            for s in range(steps):
+                t_cur = torch.full((bsz,), sched[s], device=dev, dtype=torch.bfloat16)
+                t_nxt = torch.full((bsz,), sched[s + 1], device=dev, dtype=torch.bfloat16)
+                x = self.step(x, t_cur, t_nxt, eps[s], static)
+        x_out = x
+
+        def run():
+            graph.replay()
+            return x_out
+
+        return run, graph
+
     def step(self, x, t_curr, t_next, eps, static):
         """One pingpong step (sampling.py:109-113)."""
         t_curr, t_next = self._rows(t_curr), self._rows(t_next)
