@@ -439,6 +439,37 @@ def time_w8a8(device, steps: int, warmup: int) -> dict:
             "l2": "flushed (256 MB read) before each pair"}
 
 
+def time_w8a8_glu_mlp(device, steps: int, warmup: int) -> dict:
+    """The DiT's W8A8 MLP at the 120 s clip's shape (M = 5,296 tokens, 1,024 -> 2 x 4,096 GLU -> 1,024): the GLU in
+    the first GEMM's epilogue (`hb_w8a8_gemm_glu`, then the row quantiser) against the separate GLU + quantise
+    kernel after a plain GEMM. Same bits out (tested); L2 flushed before each MLP call."""
+    import torch
+    from hummingbird_b200 import dit_glue
+    from hummingbird_b200.w8a8 import W8A8GluLinear, W8A8Linear, quantize_rows, w8a8_gemm
+    g = torch.Generator(device=device).manual_seed(12)
+    m, d, f = 5296, 1024, 4096
+    x = torch.randn(m, d, generator=g, device=device).to(torch.bfloat16)
+    w1 = (torch.randn(2 * f, d, generator=g, device=device) / d ** 0.5).to(torch.bfloat16)
+    w2 = (torch.randn(d, f, generator=g, device=device) / f ** 0.5).to(torch.bfloat16)
+    plain, fused, l2 = W8A8Linear(w1), W8A8GluLinear(w1), W8A8Linear(w2)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+
+    def unfused():
+        q, s = dit_glue.glu(plain(x), quantize=True)
+        return w8a8_gemm(q, s, l2.qw, l2.sw)
+
+    def with_epilogue():
+        q, s = quantize_rows(fused(x))
+        return w8a8_gemm(q, s, l2.qw, l2.sw)
+
+    ms_u = _event_median(unfused, steps, warmup, flush)
+    ms_f = _event_median(with_epilogue, steps, warmup, flush)
+    ops = 2.0 * m * d * 2 * f + 2.0 * m * f * d
+    return {"config": {"M": m, "d": d, "F": f}, "ms_glu_in_epilogue": ms_f, "ms_separate_glu": ms_u,
+            "tops_glu_in_epilogue": ops / (ms_f * 1e-3) / 1e12, "launches": "4 (quantise x, GEMM1+GLU, quantise z, "
+            "GEMM2) vs 4 (quantise x, GEMM1, GLU+quantise, GEMM2)", "l2": "flushed (256 MB read) before each call"}
+
+
 # ----------------------------------------------------------------------------------------------- DiT clip
 def _dit_clip_runner(model, shape, device, seed: int = 44):
     """Inputs of one clip and a `clip()` that denoises it: the whole 8-step denoise loop captured in one CUDA graph
@@ -725,6 +756,9 @@ def paths_summary(paths: dict, peaks: dict) -> dict:
         pk = d["int8_peak_tops_measured"]
         out["w8a8_c3"] = (f"g1 {d['gemm1_ms'] * 1e3:.1f} us {d['gemm1_tops']:.0f} TOPS {d['gemm1_tops'] / pk:.0%}; "
                           f"g2 {d['gemm2_ms'] * 1e3:.1f} us {d['gemm2_tops']:.0f} TOPS {d['gemm2_tops'] / pk:.0%}")
+    if "w8a8_dit_mlp" in paths:
+        d = paths["w8a8_dit_mlp"]
+        out["w8a8_mlp_120s"] = f"GLU in epilogue {d['ms_glu_in_epilogue'] * 1e3:.1f} us vs {d['ms_separate_glu'] * 1e3:.1f} us"
     for key, name in (("dit_120s_clip_bf16_mlp", "dit_120s_bf16"), ("dit_120s_clip_w8a8_mlp", "dit_120s_w8a8")):
         if key in paths:
             out[name] = f"{paths[key]['ms_per_clip']:.1f} ms/clip"
@@ -820,6 +854,7 @@ def main():
             paths["dense_120s_block_call"] = time_dense(device, 20, 3, 2, 2648, 16, 1024)
             paths["cross_120s_block_call"] = time_cross(device, 50, 5, peaks["hbm_gbs"])
             paths["w8a8_config3"] = time_w8a8(device, 50, 5)
+            paths["w8a8_dit_mlp"] = time_w8a8_glu_mlp(device, 30, 5)
             paths["dit_120s_clip_bf16_mlp"] = time_dit_clip(device, "none")
         paths["dit_120s_clip_w8a8_mlp"] = time_dit_clip(device, "w8a8", world)
         paths["band_380s_layer"] = time_band_song_layer(device, world, rank, comm=comm)

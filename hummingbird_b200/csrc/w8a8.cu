@@ -144,10 +144,19 @@ struct GemmEpi {
   int M, N, K;
 };
 
-template <int BN>
+// The GLU of `dit._feed_forward` (dit.py:218-221) in the epilogue (kGlu, BN = 256): the weight rows come
+// interleaved in blocks of 128 (value rows [128 t, 128 t + 128), then the matching gate rows), so a tile's
+// accumulator columns [0, 128) are value and [128, 256) gate columns of the same 128 outputs. Each pair is
+// rounded to bf16 as the plain epilogue would store it, then z = value * silu(gate) with silu rounded to bf16
+// and z rounded to bf16: the arithmetic of hb_glu_rows, so z is bit-identical to that kernel run on this GEMM's
+// plain output. Only z (128 columns per tile) is written.
+__device__ __forceinline__ float silu_glu(float g) { return __fdividef(g, 1.f + __expf(-g)); }
+
+template <int BN, bool kGlu = false>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     w8a8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                      const __grid_constant__ CUtensorMap tmap_out, const GemmEpi e) {
+  static_assert(!kGlu || BN == 256, "the GLU epilogue pairs 128 value with 128 gate columns");
   using C = GemmCfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
@@ -279,34 +288,67 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const float sxm = m < e.M ? e.sx[m] : 0.f;
       const uint32_t taddr = tmem + lane_base + a * BN;
       uint8_t* stage_out = smem + C::kOffOut;
+      if constexpr (kGlu) {
+        // z columns [32 c, 32 c + 32) of the tile from value chunk c and gate chunk c + 4 (two per warp)
 #pragma unroll 1
-      for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
-        uint32_t acc[32];
-        tmem_ld32(taddr + 32 * c, acc);
-        tmem_wait_ld();
-        uint32_t w[16];
+        for (int c = 2 * half; c < 2 * half + 2; ++c) {
+          uint32_t av[32], ag[32];
+          tmem_ld32(taddr + 32 * c, av);
+          tmem_ld32(taddr + 128 + 32 * c, ag);
+          tmem_wait_ld();
+          uint32_t w[16];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          float y[2];
+          for (int j = 0; j < 16; ++j) {
+            float yv[2], yg[2];
 #pragma unroll
-          for (int t = 0; t < 2; ++t) {
-            const int cc = 32 * c + 2 * j + t;
-            float v = __fmul_rn(__int2float_rn(static_cast<int>(acc[2 * j + t])), sxm);
-            v = __fmul_rn(v, psw[cc]);
-            y[t] = __fadd_rn(v, pbias[cc]);  // + 0 when there is no bias: exact
+            for (int t = 0; t < 2; ++t) {
+              const int cv = 32 * c + 2 * j + t, cg = cv + 128;
+              yv[t] = __fadd_rn(__fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(av[2 * j + t])), sxm), psw[cv]),
+                                pbias[cv]);
+              yg[t] = __fadd_rn(__fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(ag[2 * j + t])), sxm), psw[cg]),
+                                pbias[cg]);
+            }
+            const uint32_t vw = pack_bf16x2(yv[0], yv[1]), gw = pack_bf16x2(yg[0], yg[1]);
+            const float v0 = bf16_lo(vw), v1 = bf16_hi(vw), g0 = bf16_lo(gw), g1 = bf16_hi(gw);
+            const uint32_t sw2 = pack_bf16x2(silu_glu(g0), silu_glu(g1));  // silu stored as bf16
+            w[j] = pack_bf16x2(v0 * bf16_lo(sw2), v1 * bf16_hi(sw2));
           }
-          w[j] = pack_bf16x2(y[0], y[1]);
+          uint8_t* box = stage_out + (c >> 1) * (kBM * 128);
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            *reinterpret_cast<uint4*>(box + sw128_offset(r, (c & 1) * 4 + j)) =
+                make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
         }
-        // 32 columns = half of a 64-column box: 4 16-byte chunks of this row in the swizzled staging
-        uint8_t* box = stage_out + (c >> 1) * (kBM * 128);
+      } else {
+#pragma unroll 1
+        for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
+          uint32_t acc[32];
+          tmem_ld32(taddr + 32 * c, acc);
+          tmem_wait_ld();
+          uint32_t w[16];
 #pragma unroll
-        for (int j = 0; j < 4; ++j)
-          *reinterpret_cast<uint4*>(box + sw128_offset(r, (c & 1) * 4 + j)) =
-              make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
-        if (e.acc_out && m < e.M && n0 + 32 * c < e.N) {
-          uint4* a4 = reinterpret_cast<uint4*>(e.acc_out + (size_t)m * e.ldacc + n0 + 32 * c);
+          for (int j = 0; j < 16; ++j) {
+            float y[2];
 #pragma unroll
-          for (int j = 0; j < 8; ++j) a4[j] = make_uint4(acc[4 * j], acc[4 * j + 1], acc[4 * j + 2], acc[4 * j + 3]);
+            for (int t = 0; t < 2; ++t) {
+              const int cc = 32 * c + 2 * j + t;
+              float v = __fmul_rn(__int2float_rn(static_cast<int>(acc[2 * j + t])), sxm);
+              v = __fmul_rn(v, psw[cc]);
+              y[t] = __fadd_rn(v, pbias[cc]);  // + 0 when there is no bias: exact
+            }
+            w[j] = pack_bf16x2(y[0], y[1]);
+          }
+          // 32 columns = half of a 64-column box: 4 16-byte chunks of this row in the swizzled staging
+          uint8_t* box = stage_out + (c >> 1) * (kBM * 128);
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            *reinterpret_cast<uint4*>(box + sw128_offset(r, (c & 1) * 4 + j)) =
+                make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+          if (e.acc_out && m < e.M && n0 + 32 * c < e.N) {
+            uint4* a4 = reinterpret_cast<uint4*>(e.acc_out + (size_t)m * e.ldacc + n0 + 32 * c);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) a4[j] = make_uint4(acc[4 * j], acc[4 * j + 1], acc[4 * j + 2], acc[4 * j + 3]);
+          }
         }
       }
       // accumulator fully read: release it to the MMA thread
@@ -317,9 +359,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       fence_proxy_async_smem();
       asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory");
       if (et == 0) {
+        if constexpr (kGlu) {  // 128 z columns at z column n0 / 2
 #pragma unroll 1
-        for (int bx = 0; bx < BN / 64; ++bx)
-          if (n0 + 64 * bx < e.N) tma_store_2d(&tmap_out, n0 + 64 * bx, m0, stage_out + bx * (kBM * 128));
+          for (int bx = 0; bx < 2; ++bx) tma_store_2d(&tmap_out, n0 / 2 + 64 * bx, m0, stage_out + bx * (kBM * 128));
+        } else {
+#pragma unroll 1
+          for (int bx = 0; bx < BN / 64; ++bx)
+            if (n0 + 64 * bx < e.N) tma_store_2d(&tmap_out, n0 + 64 * bx, m0, stage_out + bx * (kBM * 128));
+        }
         bulk_commit_group();
       }
       if (et == 0) GTRACE(2, 200 + local, t0);
@@ -589,22 +636,22 @@ bool make_tmap_out(CUtensorMap* map, void* base, int M, int N, int64_t ldo) {
          CUDA_SUCCESS;
 }
 
-template <int BN>
+template <int BN, bool kGlu = false>
 int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to, const GemmEpi& e,
                 cudaStream_t stream) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return HB_ERR_LAUNCH;
   static bool configured[64] = {};
   if (dev < 64 && !configured[dev]) {
-    if (cudaFuncSetAttribute(w8a8_gemm_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, GemmCfg<BN>::kSmem) !=
-        cudaSuccess)
+    if (cudaFuncSetAttribute(w8a8_gemm_kernel<BN, kGlu>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             GemmCfg<BN>::kSmem) != cudaSuccess)
       return HB_ERR_LAUNCH;
     configured[dev] = true;
   }
   int sms = 148;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int tiles = ((e.M + kBM - 1) / kBM) * ((e.N + BN - 1) / BN);
-  w8a8_gemm_kernel<BN><<<tiles < sms ? tiles : sms, kGemmThreads, GemmCfg<BN>::kSmem, stream>>>(ta, tb, to, e);
+  w8a8_gemm_kernel<BN, kGlu><<<tiles < sms ? tiles : sms, kGemmThreads, GemmCfg<BN>::kSmem, stream>>>(ta, tb, to, e);
   return cudaGetLastError() == cudaSuccess ? HB_OK : HB_ERR_LAUNCH;
 }
 
@@ -682,4 +729,20 @@ extern "C" int hb_w8a8_gemm(const void* qx, int64_t ldqx, const float* sx, const
   const bool wide = (N % 256 == 0) && ((long)((M + kBM - 1) / kBM) * (N / 256) >= 148);
   if (!make_tmap_i8(&tb, qw, N, K, ldqw, wide ? 256 : 128)) return HB_ERR_LAUNCH;
   return wide ? launch_gemm<256>(ta, tb, to, e, stream) : launch_gemm<128>(ta, tb, to, e, stream);
+}
+
+extern "C" int hb_w8a8_gemm_glu(const void* qx, int64_t ldqx, const float* sx, const void* qw, int64_t ldqw,
+                                const float* sw, const void* bias, void* z, int64_t ldz, int M, int F, int K,
+                                cudaStream_t stream) {
+  if (!qx || !sx || !qw || !sw || !z) return HB_ERR_NULL;
+  if (M < 1 || F < 128 || F % 128 || K < 16 || K % 16 || ldqx < K || ldqw < K || ldz < F) return HB_ERR_SHAPE;
+  if (!aligned16(qx) || ldqx % 16 || !aligned16(qw) || ldqw % 16 || !aligned16(z) || ldz % 8) return HB_ERR_ALIGN;
+  int st = check_device();
+  if (st != HB_OK) return st;
+  GemmEpi e{sx, sw, static_cast<const uint16_t*>(bias), static_cast<uint16_t*>(z), ldz, nullptr, 0, M, 2 * F, K};
+  CUtensorMap ta, tb, to;
+  if (!make_tmap_i8(&ta, qx, M, K, ldqx, kBM)) return HB_ERR_LAUNCH;
+  if (!make_tmap_i8(&tb, qw, 2 * F, K, ldqw, 256)) return HB_ERR_LAUNCH;
+  if (!make_tmap_out(&to, z, M, F, ldz)) return HB_ERR_LAUNCH;
+  return launch_gemm<256, true>(ta, tb, to, e, stream);
 }

@@ -35,7 +35,7 @@ from hummingbird_b200 import dense_attention as hb_dense
 from hummingbird_b200 import dit_glue as glue
 from hummingbird_b200 import parallel as par
 from hummingbird_b200.config import DiTConfig
-from hummingbird_b200.w8a8 import W8A8Linear, w8a8_gemm
+from hummingbird_b200.w8a8 import W8A8GluLinear, W8A8Linear, quantize_rows, w8a8_gemm
 
 
 @dataclass(frozen=True)
@@ -152,6 +152,7 @@ class DiT:
                 b["self_attn"]["to_qkv_dest"] = b["self_attn"]["to_qkv"][rows].view(self.world, -1, d).transpose(1, 2)
             if cfg.ff_quant == "w8a8":
                 b["glu_q"] = W8A8Linear(b["glu"]["w"], b["glu"]["b"])
+                b["glu_fused"] = W8A8GluLinear(b["glu"]["w"], b["glu"]["b"])
                 b["proj_out_q"] = W8A8Linear(b["proj_out"]["w"], b["proj_out"]["b"])
             self.blocks.append(b)
 
@@ -321,11 +322,12 @@ class DiT:
     def _ff(self, x, b):
         """`dit._feed_forward`: GLU `value * silu(gate)` (dit.py:218-221), W8A8 or bf16."""
         if self.cfg.ff_quant == "w8a8":
-            g = b["glu_q"](x)
-            if self.glue == "cuda":  # value * silu(gate) and the per-token quantisation in one pass
-                q, s = glue.glu(g, quantize=True)
+            if self.glue == "cuda":  # value * silu(gate) in the first GEMM's epilogue, then the per-token quantiser
+                z = b["glu_fused"](x)
+                q, s = quantize_rows(z.reshape(-1, z.shape[-1]))
                 po = b["proj_out_q"]
                 return w8a8_gemm(q, s, po.qw, po.sw, po.bias).view(*x.shape[:-1], -1)
+            g = b["glu_q"](x)
             value, gate = g.chunk(2, -1)
             return b["proj_out_q"](value * F.silu(gate))
         g = x @ b["glu"]["w"].T + b["glu"]["b"]

@@ -58,3 +58,48 @@ class W8A8Linear:
         x2 = x.reshape(-1, self.in_features).to(torch.bfloat16)
         qx, sx = quantize_rows(x2)
         return w8a8_gemm(qx, sx, self.qw, self.sw, self.bias).reshape(*lead, self.out_features)
+
+
+def glu_interleave(t: torch.Tensor) -> torch.Tensor:
+    """Rows (dim 0) of a GLU projection `[value (F) | gate (F)]` reordered in blocks of 128: value rows
+    [128 t, 128 t + 128), then gate rows [F + 128 t, F + 128 t + 128), for t = 0 .. F / 128 - 1 — the order
+    `hb_w8a8_gemm_glu` reads (each 256-column output tile holds matching value and gate columns)."""
+    two_f = t.shape[0]
+    f = two_f // 2
+    if two_f % 256:
+        raise ValueError("the GLU width F must be a multiple of 128")
+    blocks = t.reshape(2, f // 128, 128, *t.shape[1:])
+    return blocks.transpose(0, 1).reshape(two_f, *t.shape[1:]).contiguous()
+
+
+def w8a8_gemm_glu(qx: torch.Tensor, sx: torch.Tensor, qw: torch.Tensor, sw: torch.Tensor,
+                  bias: torch.Tensor | None = None, *, out: torch.Tensor | None = None) -> torch.Tensor:
+    """z = value * silu(gate) of the W8A8 GEMM `qx @ qw^T` whose weight rows are in `glu_interleave` order."""
+    check_cuda(qx, sx, qw, sw)
+    m, k = qx.shape
+    f = qw.shape[0] // 2
+    if qw.shape[1] != k:
+        raise ValueError("qx and qw must share K")
+    if bias is not None:
+        bias = bias.to(torch.bfloat16).contiguous()
+    out = torch.empty(m, f, dtype=torch.bfloat16, device=qx.device) if out is None else out
+    _lib.call("hb_w8a8_gemm_glu", ptr(qx), qx.stride(0), ptr(sx), ptr(qw), qw.stride(0), ptr(sw), ptr(bias), ptr(out),
+              out.stride(0), m, f, k, stream_handle(qx.device))
+    return out
+
+
+class W8A8GluLinear:
+    """The MLP's GLU projection (`glu_proj`, weight `[2F, in]` = [value | gate] rows) run as W8A8 with
+    `value * silu(gate)` in the GEMM epilogue: `__call__(x)` returns z `[..., F]` in bf16."""
+
+    def __init__(self, weight: torch.Tensor, bias: torch.Tensor | None = None):
+        w = glu_interleave(weight.to(torch.bfloat16))
+        self.qw, self.sw = quantize_rows(w)
+        self.bias = None if bias is None else glu_interleave(bias.to(torch.bfloat16))
+        self.out_features, self.in_features = weight.shape[0] // 2, weight.shape[1]
+
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        lead = x.shape[:-1]
+        x2 = x.reshape(-1, self.in_features).to(torch.bfloat16)
+        qx, sx = quantize_rows(x2)
+        return w8a8_gemm_glu(qx, sx, self.qw, self.sw, self.bias).reshape(*lead, self.out_features)

@@ -150,6 +150,20 @@ int hb_w8a8_gemm(const void* qx, int64_t ldqx, const float* sx, const void* qw, 
                  const void* bias, void* out, int64_t ldo, int32_t* acc_out, int64_t ldacc, int M, int N, int K,
                  cudaStream_t stream);
 
+/* The MLP's first GEMM with its GLU in the epilogue (`dit._feed_forward`, dit.py:218-221:
+ * z = value * silu(gate) of `_linear(x, glu_proj)`), writing only z bf16 [M, F] (ld ldz elements).
+ *   qw   int8 [2F, K] weight rows interleaved in blocks of 128: rows [256 t, 256 t + 128) are value rows
+ *        [128 t, 128 t + 128) of the checkpoint's `glu_proj` weight [2F, K] (value = its first F rows) and rows
+ *        [256 t + 128, 256 t + 256) the matching gate rows [F + 128 t, F + 128 t + 128); sw fp32 [2F] and bias
+ *        bf16 [2F] (or NULL) in the same order. `hummingbird_b200.w8a8.glu_interleave` builds the order.
+ * z equals, bit for bit, hb_glu_rows (bf16 mode) applied to hb_w8a8_gemm's output with the plain row order:
+ * value and gate rounded to bf16 as that GEMM stores them, silu rounded to bf16, z rounded to bf16. Quantise z
+ * with hb_quant_rows_int8 for the MLP's second GEMM (bit-identical to hb_glu_rows' int8 mode).
+ * F a multiple of 128, K a multiple of 16. No reference counterpart as an entry point (the reference's MLP is a
+ * bf16 matmul, then separate XLA ops for the GLU). */
+int hb_w8a8_gemm_glu(const void* qx, int64_t ldqx, const float* sx, const void* qw, int64_t ldqw, const float* sw,
+                     const void* bias, void* z, int64_t ldz, int M, int F, int K, cudaStream_t stream);
+
 /* ---- DiT block glue (the elementwise steps around the kernels above) ------------------------------------ */
 /* No reference counterpart as entry points: the reference runs these steps as separate XLA ops inside
  * `dit._block` (dit.py:224-250); here each fuses several of them into one pass over the activation rows.

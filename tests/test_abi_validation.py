@@ -174,6 +174,21 @@ def test_w8a8_gemm_rejects(lib, override, status):
     assert lib.hb_w8a8_gemm(*_gemm(**override)) == status
 
 
+def test_w8a8_gemm_glu_rejects(lib):
+    # qx, ldqx, sx, qw, ldqw, sw, bias, z, ldz, M, F, K, stream: the GLU width F comes in 128-column blocks
+    ok = dict(qx=P, ldqx=1024, sx=P, qw=P, ldqw=1024, sw=P, bias=None, z=P, ldz=4096, M=5296, F=4096, K=1024, s=None)
+
+    def call(**kw):
+        a = dict(ok)
+        a.update(kw)
+        return lib.hb_w8a8_gemm_glu(*a.values())
+    assert call(F=4032, ldz=4032) == _lib.HB_ERR_SHAPE
+    assert call(ldz=4000) == _lib.HB_ERR_SHAPE
+    assert call(K=1000, ldqx=1008, ldqw=1008) == _lib.HB_ERR_SHAPE
+    assert call(qw=P + 8) == _lib.HB_ERR_ALIGN
+    assert call(z=None) == _lib.HB_ERR_NULL
+
+
 def test_quantiser_rejects(lib):
     assert lib.hb_quant_rows_int8(P, 1024, 2584, 12, P, 1024, P, None) == _lib.HB_ERR_SHAPE
     assert lib.hb_quant_rows_int8(P, 1024, 2584, 1024, P + 4, 1024, P, None) == _lib.HB_ERR_ALIGN

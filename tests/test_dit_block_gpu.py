@@ -20,7 +20,7 @@ pytestmark = pytest.mark.gpu
 def _model_with_golden_block(z, ff_quant: str, glue: str):
     from hummingbird_b200.config import DiTConfig
     from hummingbird_b200.dit import ClipShape, DiT
-    from hummingbird_b200.w8a8 import W8A8Linear
+    from hummingbird_b200.w8a8 import W8A8GluLinear, W8A8Linear
     heads, memory = int(z["heads"]), int(z["memory"])
     batch, length, d = z["h_bits"].shape
     cfg = DiTConfig(embed_dim=d, num_heads=heads, num_memory_tokens=memory, ff_quant=ff_quant,
@@ -44,6 +44,7 @@ def _model_with_golden_block(z, ff_quant: str, glue: str):
     b["proj_out"] = {"w": w["proj_w"], "b": w["proj_b"]}
     if ff_quant == "w8a8":
         b["glu_q"] = W8A8Linear(w["glu_w"], w["glu_b"])
+        b["glu_fused"] = W8A8GluLinear(w["glu_w"], w["glu_b"])
         b["proj_out_q"] = W8A8Linear(w["proj_w"], w["proj_b"])
     model.p["rope_inv_freq"] = torch.from_numpy(z["inv_freq"]).cuda()
     return model, b

@@ -69,3 +69,30 @@ def test_w8a8_linear_pair_config3(cuda_lib):
     assert np.array_equal(bits_np(h), h_ref)
     y_ref, _, _, _ = ow.w8a8_linear(h_ref, l2.qw.cpu().numpy(), l2.sw.cpu().numpy(), bits_np(w.b2))
     assert np.array_equal(bits_np(y), y_ref)
+
+
+@pytest.mark.parametrize("m,k,f", [(2584, 1024, 4096), (5296, 1024, 4096), (200, 96, 256), (129, 1040, 384)])
+def test_w8a8_gemm_glu_epilogue_bit_exact(cuda_lib, m, k, f):
+    """The GEMM with the GLU in its epilogue (`hb_w8a8_gemm_glu`, weight rows in `glu_interleave` order) against
+    the unfused sequence it replaces: the plain GEMM's bf16 output, then `hb_glu_rows`. z is bit-identical, and so
+    is its per-row int8 form (`hb_quant_rows_int8` on the fused z against `hb_glu_rows`' int8 mode). Ragged M,
+    K past whole 128-byte stages, and F of one to 32 value/gate tile pairs."""
+    from hummingbird_b200 import _lib, dit_glue
+    from hummingbird_b200.w8a8 import W8A8GluLinear, glu_interleave, quantize_rows, w8a8_gemm
+    g = torch.Generator(device="cuda").manual_seed(m + k + f)
+    x = torch.randn(m, k, generator=g, device="cuda").to(torch.bfloat16)
+    w = (torch.randn(2 * f, k, generator=g, device="cuda") / k ** 0.5).to(torch.bfloat16)
+    bias = (0.05 * torch.randn(2 * f, generator=g, device="cuda")).to(torch.bfloat16)
+    qx, sx = quantize_rows(x)
+    qw, sw = quantize_rows(w)
+    plain = w8a8_gemm(qx, sx, qw, sw, bias)
+    z_ref = dit_glue.glu(plain)
+    q_ref, s_ref = dit_glue.glu(plain, quantize=True)
+    lin = W8A8GluLinear(w, bias)
+    assert torch.equal(lin.qw, glu_interleave(qw)) and torch.equal(lin.sw, glu_interleave(sw))
+    z = lin(x)
+    q, s = quantize_rows(z)
+    torch.cuda.synchronize()
+    assert np.array_equal(bits_np(z), bits_np(z_ref))
+    assert torch.equal(q, q_ref) and torch.equal(s, s_ref)
+    assert _lib.device_status() == 0
