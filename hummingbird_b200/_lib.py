@@ -37,6 +37,7 @@ SIGNATURES: dict[str, list] = {
     "hb_w8a8_gemm": [_p, _i64, _p, _p, _i64, _p, _p, _p, _i64, _p, _i64, _i, _i, _i, _p],
     "hb_w8a8_gemm_glu": [_p, _i64, _p, _p, _i64, _p, _p, _p, _i64, _i, _i, _i, _p],
     "hb_dit_residual_norm": [_p, _i64, _p, _i64, _p, _p, _p, _i64, _p, _i, _p, _p, _i64, _i, _i, _i, _f, _p],
+    "hb_dit_residual_norm_int8": [_p, _i64, _p, _i64, _p, _p, _p, _i64, _p, _i, _p, _p, _i64, _p, _i, _i, _i, _f, _p],
     "hb_glu_rows": [_p, _i64, _i, _i, _p, _i64, _p, _i64, _p, _p],
     "hb_head_rms_norm": [_p, _i64, _i, _i, _p, _f, _p, _i64, _p],
 }

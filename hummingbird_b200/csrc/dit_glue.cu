@@ -54,6 +54,9 @@ struct ResNormParams {
   int64_t ldx;
   int rows, rows_per_batch, d;
   float eps;
+  int8_t* xq;         // optional: x quantised per row (hb_quant_rows_int8's rules on the bf16 x) ...
+  int64_t ldxq;
+  float* xscale;      // ... and its per-row scales
 };
 
 constexpr int kRowWarps = 8;
@@ -108,24 +111,46 @@ __device__ __forceinline__ void residual_norm_row(const ResNormParams& p, const 
 #pragma unroll
     for (int e = 0; e < 8; ++e) ss = fmaf(v[i][e], v[i][e], ss);
   }
-  if (!p.x) return;
+  if (!p.x && !p.xq) return;
 #pragma unroll
   for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
   const float inv = rsqrtf(ss / static_cast<float>(d) + p.eps);
-  uint16_t* xr = p.x + (size_t)r * p.ldx;
+  // x = RMSNorm(h) * w (rounded to bf16), then (1 + scale) and shift; the bf16 rounding of the store is applied
+  // here too, so the quantised form sees exactly the values of the bf16 x
+  float (&o)[NC][8] = v;  // x overwrites the residual row in registers (h is stored already)
 #pragma unroll
   for (int i = 0; i < NC; ++i) {
     const int c = (i * 32 + lane) * 8;
-    float o[8];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) o[e] = __fmul_rn(v[i][e], inv) * wv[c + e];
+    for (int e = 0; e < 8; ++e) o[i][e] = __fmul_rn(v[i][e], inv) * wv[c + e];
 #pragma unroll
-    for (int e = 0; e < 8; e += 2) round_bf16_pair(o[e], o[e + 1]);
+    for (int e = 0; e < 8; e += 2) round_bf16_pair(o[i][e], o[i][e + 1]);
     if (p.scale) {
 #pragma unroll
-      for (int e = 0; e < 8; ++e) o[e] = shv[c + e] + o[e] * sc1[c + e];
+      for (int e = 0; e < 8; ++e) o[i][e] = __fadd_rn(shv[c + e], __fmul_rn(o[i][e], sc1[c + e]));
     }
-    *reinterpret_cast<uint4*>(xr + c) = pack8(o);
+#pragma unroll
+    for (int e = 0; e < 8; e += 2) round_bf16_pair(o[i][e], o[i][e + 1]);
+    if (p.x) *reinterpret_cast<uint4*>(p.x + (size_t)r * p.ldx + c) = pack8(o[i]);
+  }
+  if (!p.xq) return;
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < NC; ++i)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(o[i][e]));
+#pragma unroll
+  for (int s2 = 16; s2; s2 >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, s2));
+  const float s = amax == 0.f ? 1.f : __fdiv_rn(amax, 127.f);
+  const float rs = __frcp_rn(s);
+  if (lane == 0) p.xscale[r] = s;
+#pragma unroll
+  for (int i = 0; i < NC; ++i) {
+    const int c = (i * 32 + lane) * 8;
+    uint32_t packed[2] = {0u, 0u};
+#pragma unroll
+    for (int e = 0; e < 8; ++e) packed[e >> 2] |= int8_bits(quantize_int8(o[i][e], s, rs)) << (8 * (e & 3));
+    *reinterpret_cast<uint2*>(p.xq + (size_t)r * p.ldxq + c) = make_uint2(packed[0], packed[1]);
   }
 }
 
@@ -164,7 +189,7 @@ __global__ void __launch_bounds__(32 * kRowWarps, kStreamBlocksPerSm)
         cv[c + e] = round_bf16(1.f / (1.f + __expf(-a)));
       }
     }
-    if (p.x) {
+    if (p.x || p.xq) {
       unpack8(ld_v4(p.w + c), u);
 #pragma unroll
       for (int e = 0; e < 8; ++e) cv[d + c + e] = u[e];
@@ -335,25 +360,28 @@ __global__ void __launch_bounds__(256) head_rms_kernel(const uint16_t* __restric
 
 using namespace hb;
 
-extern "C" int hb_dit_residual_norm(void* h, int64_t ldh, const void* y, int64_t ldy, const void* gate,
-                                    const void* scale, const void* shift, int64_t ldc, const void* local,
-                                    int local_row0, const void* weight, void* x, int64_t ldx, int rows,
-                                    int rows_per_batch, int d, float eps, cudaStream_t stream) {
-  if (!h || (x && !weight) || (scale && !shift) || (!scale && shift)) return HB_ERR_NULL;
+namespace {
+
+int residual_norm_entry(void* h, int64_t ldh, const void* y, int64_t ldy, const void* gate, const void* scale,
+                        const void* shift, int64_t ldc, const void* local, int local_row0, const void* weight, void* x,
+                        int64_t ldx, void* q, int64_t ldq, float* qscale, int rows, int rows_per_batch, int d,
+                        float eps, cudaStream_t stream) {
+  if (!h || ((x || q) && !weight) || (scale && !shift) || (!scale && shift) || (q && !qscale)) return HB_ERR_NULL;
   if (rows < 1 || rows_per_batch < 1 || d < 256 || d > 2048 || d % 256 || ldh < d || (y && ldy < d) ||
-      (x && ldx < d) || ((gate || scale) && ldc < d) || (gate && !y))
+      (x && ldx < d) || (q && ldq < d) || ((gate || scale) && ldc < d) || (gate && !y))
     return HB_ERR_SHAPE;
   const void* ptrs[] = {h, y, gate, scale, shift, local, weight, x};
-  for (const void* q : ptrs)
-    if (q && !aligned16(q)) return HB_ERR_ALIGN;
+  for (const void* pp : ptrs)
+    if (pp && !aligned16(pp)) return HB_ERR_ALIGN;
   if (ldh % 8 || (y && ldy % 8) || (x && ldx % 8) || ldc % 8) return HB_ERR_ALIGN;
+  if (q && ((reinterpret_cast<uintptr_t>(q) & 7u) || ldq % 8)) return HB_ERR_ALIGN;
   int st = check_device();
   if (st != HB_OK) return st;
   ResNormParams p{static_cast<uint16_t*>(h), ldh, static_cast<const uint16_t*>(y), ldy,
                   static_cast<const uint16_t*>(gate), static_cast<const uint16_t*>(scale),
                   static_cast<const uint16_t*>(shift), ldc, static_cast<const uint16_t*>(local), local_row0,
                   static_cast<const uint16_t*>(weight), static_cast<uint16_t*>(x), ldx, rows, rows_per_batch, d,
-                  eps};
+                  eps, static_cast<int8_t*>(q), ldq, qscale};
   switch (d / 256) {
     case 1: return launch_residual_norm<1>(p, stream);
     case 2: return launch_residual_norm<2>(p, stream);
@@ -364,6 +392,25 @@ extern "C" int hb_dit_residual_norm(void* h, int64_t ldh, const void* y, int64_t
     case 7: return launch_residual_norm<7>(p, stream);
     default: return launch_residual_norm<8>(p, stream);
   }
+}
+
+}  // namespace
+
+extern "C" int hb_dit_residual_norm(void* h, int64_t ldh, const void* y, int64_t ldy, const void* gate,
+                                    const void* scale, const void* shift, int64_t ldc, const void* local,
+                                    int local_row0, const void* weight, void* x, int64_t ldx, int rows,
+                                    int rows_per_batch, int d, float eps, cudaStream_t stream) {
+  return residual_norm_entry(h, ldh, y, ldy, gate, scale, shift, ldc, local, local_row0, weight, x, ldx, nullptr, 0,
+                             nullptr, rows, rows_per_batch, d, eps, stream);
+}
+
+extern "C" int hb_dit_residual_norm_int8(void* h, int64_t ldh, const void* y, int64_t ldy, const void* gate,
+                                         const void* scale, const void* shift, int64_t ldc, const void* local,
+                                         int local_row0, const void* weight, void* q, int64_t ldq, float* qscale,
+                                         int rows, int rows_per_batch, int d, float eps, cudaStream_t stream) {
+  if (!q) return HB_ERR_NULL;
+  return residual_norm_entry(h, ldh, y, ldy, gate, scale, shift, ldc, local, local_row0, weight, nullptr, 0, q, ldq,
+                             qscale, rows, rows_per_batch, d, eps, stream);
 }
 
 extern "C" int hb_glu_rows(const void* glu, int64_t ldg, int rows, int F, void* z, int64_t ldz, void* q, int64_t ldq,

@@ -274,9 +274,15 @@ class DiT:
             y = self._self_attn(x, b["self_attn"], static) @ b["self_attn"]["to_out"].T
             x = glue.residual_norm(h, y=y, gate=part(c, 2), weight=b["cross_attend_norm_bf"], eps=eps)
             y = self._cross_fused(x, b["cross_attn"], static["cross_kv_rows"][i])
-            x = glue.residual_norm(h, y=y, local=b["local"], local_row0=self.mem_rows, weight=b["ff_norm_bf"],
-                                   scale=part(c, 3), shift=part(c, 4), eps=eps)
-            y = self._ff(x, b)
+            if self.cfg.ff_quant == "w8a8":  # the MLP's input leaves the norm kernel already quantised per token
+                qx, sx = glue.residual_norm(h, y=y, local=b["local"], local_row0=self.mem_rows,
+                                            weight=b["ff_norm_bf"], scale=part(c, 3), shift=part(c, 4), eps=eps,
+                                            quantize=True)
+                y = self._ff_quantized(qx, sx, b, h.shape[:-1])
+            else:
+                x = glue.residual_norm(h, y=y, local=b["local"], local_row0=self.mem_rows, weight=b["ff_norm_bf"],
+                                       scale=part(c, 3), shift=part(c, 4), eps=eps)
+                y = self._ff(x, b)
             if i + 1 < len(self.blocks):
                 nb, nc = self.blocks[i + 1], conds[i + 1]
                 x = glue.residual_norm(h, y=y, gate=part(c, 5), weight=nb["pre_norm_bf"], scale=part(nc, 0),
@@ -318,6 +324,14 @@ class DiT:
         k, kd, v = kv
         out = F.scaled_dot_product_attention(q, k, v) - F.scaled_dot_product_attention(qd, kd, v)
         return out.transpose(1, 2).reshape(bsz, length, -1) @ ca["to_out"].T
+
+    def _ff_quantized(self, qx, sx, b, lead):
+        """The W8A8 MLP from its per-token quantised input: GEMM1 with the GLU in its epilogue, the quantiser,
+        GEMM2."""
+        z = b["glu_fused"].quantized(qx, sx)
+        q, s = quantize_rows(z)
+        po = b["proj_out_q"]
+        return w8a8_gemm(q, s, po.qw, po.sw, po.bias).view(*lead, -1)
 
     def _ff(self, x, b):
         """`dit._feed_forward`: GLU `value * silu(gate)` (dit.py:218-221), W8A8 or bf16."""

@@ -23,10 +23,12 @@ def _rows(t: torch.Tensor) -> torch.Tensor:
 def residual_norm(h: torch.Tensor, *, y: torch.Tensor | None = None, gate: torch.Tensor | None = None,
                   local: torch.Tensor | None = None, local_row0: int = 0, weight: torch.Tensor | None = None,
                   scale: torch.Tensor | None = None, shift: torch.Tensor | None = None, eps: float = 1e-5,
-                  out: torch.Tensor | None = None) -> torch.Tensor | None:
+                  out: torch.Tensor | None = None, quantize: bool = False):
     """In place on `h` `(B, T, d)`: `h += y * sigmoid(1 - gate)` (gate `(B, d)`, optional), `h[:, t >= local_row0]
     += local`; then, if `weight` is given, returns `RMSNorm(h) * weight * (1 + scale) + shift` (scale, shift
-    `(B, d)`, optional). `gate`, `scale`, `shift` may be column slices of one `(B, k * d)` tensor."""
+    `(B, d)`, optional). `gate`, `scale`, `shift` may be column slices of one `(B, k * d)` tensor. With
+    `quantize`, that result comes per row in int8 form for a W8A8 GEMM: `(q (B * T, d) int8, scale (B * T,) fp32)`,
+    exactly `w8a8.quantize_rows` of the bf16 result."""
     bsz, t, d = h.shape
     if not h.is_contiguous():
         raise ValueError("h must be contiguous")
@@ -37,6 +39,15 @@ def residual_norm(h: torch.Tensor, *, y: torch.Tensor | None = None, gate: torch
         if c.shape != (bsz, d) or c.stride() != (ldc, 1) or c.dtype != torch.bfloat16:
             raise ValueError("gate / scale / shift must be (B, d) bf16 rows of one common stride")
     y2 = None if y is None else _rows(y)
+    if quantize:
+        if weight is None:
+            raise ValueError("the quantised output is the normalised x: weight is required")
+        q = torch.empty(bsz * t, d, dtype=torch.int8, device=h.device)
+        qs = torch.empty(bsz * t, dtype=torch.float32, device=h.device)
+        _lib.call("hb_dit_residual_norm_int8", ptr(h), d, ptr(y2), 0 if y2 is None else y2.stride(0), ptr(gate),
+                  ptr(scale), ptr(shift), ldc, ptr(local), local_row0, ptr(weight), ptr(q), d, ptr(qs), bsz * t, t, d,
+                  float(eps), stream_handle(h.device))
+        return q, qs
     x = None
     if weight is not None:
         x = torch.empty_like(h) if out is None else out

@@ -103,3 +103,7 @@ class W8A8GluLinear:
         x2 = x.reshape(-1, self.in_features).to(torch.bfloat16)
         qx, sx = quantize_rows(x2)
         return w8a8_gemm_glu(qx, sx, self.qw, self.sw, self.bias).reshape(*lead, self.out_features)
+
+    def quantized(self, qx: torch.Tensor, sx: torch.Tensor) -> torch.Tensor:
+        """z `(rows, F)` from an activation already quantised per row (`quantize_rows` form)."""
+        return w8a8_gemm_glu(qx, sx, self.qw, self.sw, self.bias)

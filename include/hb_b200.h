@@ -181,6 +181,15 @@ int hb_dit_residual_norm(void* h, int64_t ldh, const void* y, int64_t ldy, const
                          const void* shift, int64_t ldc, const void* local, int local_row0, const void* weight,
                          void* x, int64_t ldx, int rows, int rows_per_batch, int d, float eps, cudaStream_t stream);
 
+/* hb_dit_residual_norm with the normalised, modulated x written quantised per row instead of as bf16: q int8
+ * [rows, d] (ld ldq bytes, 8-byte aligned rows) and qscale fp32 [rows], by hb_quant_rows_int8's rules applied to
+ * the bf16 x (bit-identical to running that quantiser on hb_dit_residual_norm's x). Feeds a W8A8 GEMM (the MLP,
+ * dit.py:246-249) without a separate quantiser pass. Same arguments otherwise (weight required). */
+int hb_dit_residual_norm_int8(void* h, int64_t ldh, const void* y, int64_t ldy, const void* gate, const void* scale,
+                              const void* shift, int64_t ldc, const void* local, int local_row0, const void* weight,
+                              void* q, int64_t ldq, float* qscale, int rows, int rows_per_batch, int d, float eps,
+                              cudaStream_t stream);
+
 /* GLU of `dit._feed_forward` (dit.py:218-221): per row of glu [rows, 2F] (value = columns [0, F), gate =
  * [F, 2F)), z = value * silu(gate) rounded to bf16; written to z [rows, F] (ld ldz) OR quantised per row
  * with hb_quant_rows_int8's rules into q int8 [rows, F] (ld ldq bytes) and scale fp32 [rows] (exactly one

@@ -209,6 +209,17 @@ def test_glue_entry_points_reject(lib):
     assert res(scale=P) == _lib.HB_ERR_NULL              # adaLN scale without shift
     assert res(weight=None) == _lib.HB_ERR_NULL          # a normed output needs the norm weight
     assert res(local=MIS) == _lib.HB_ERR_ALIGN
+    # the int8 form: h, ldh, y, ldy, gate, scale, shift, ldc, local, row0, weight, q, ldq, qscale, rows, rpb, d, eps
+    def res_q(**kw):
+        a = dict(h=P, ldh=1024, y=P, ldy=1024, gate=P, scale=None, shift=None, ldc=6144, local=None, row0=0,
+                 weight=P, q=P, ldq=1024, qs=P, rows=5296, rpb=2648, d=1024, eps=1e-6, stream=None)
+        a.update(kw)
+        return lib.hb_dit_residual_norm_int8(*a.values())
+    assert res_q(qs=None) == _lib.HB_ERR_NULL             # int8 rows need their scales
+    assert res_q(q=None) == _lib.HB_ERR_NULL
+    assert res_q(weight=None) == _lib.HB_ERR_NULL
+    assert res_q(q=P + 4) == _lib.HB_ERR_ALIGN
+    assert res_q(ldq=1000) == _lib.HB_ERR_SHAPE
     # GLU: glu, ldg, rows, F, z, ldz, q, ldq, scale, stream
     assert lib.hb_glu_rows(P, 8192, 5296, 4096, P, 4096, P, 4096, P, None) == _lib.HB_ERR_NULL   # z or q, not both
     assert lib.hb_glu_rows(P, 8192, 5296, 4096, None, 0, P, 4096, None, None) == _lib.HB_ERR_NULL  # q needs scales

@@ -126,3 +126,27 @@ def test_dit_step_fused_glue_matches_torch_glue(cuda_lib, ff_quant):
         outs.append(model.step(x, t, tn, eps, model.prepare_static(cross, glob)).float())
     rel = ((outs[0] - outs[1]).norm() / outs[1].norm()).item()
     assert torch.isfinite(outs[0]).all() and rel < 2e-2, f"relative difference {rel:.3e}"
+
+
+@pytest.mark.parametrize("d,mods", [(1024, "all"), (1024, "none"), (256, "gate_only"), (1536, "all")])
+def test_residual_norm_int8_output_matches_quantiser(cuda_lib, d, mods):
+    """`hb_dit_residual_norm_int8` writes the normalised, modulated x quantised per row: the same int8 values and
+    scales as `quantize_rows` on the bf16 x of `hb_dit_residual_norm`, and the same updated h."""
+    from hummingbird_b200 import dit_glue
+    from hummingbird_b200.w8a8 import quantize_rows
+    g = torch.Generator(device="cuda").manual_seed(d)
+    bsz, t = 2, 300
+    bf = lambda *s: torch.randn(*s, generator=g, device="cuda").to(torch.bfloat16)  # noqa: E731
+    h0, y, cond, w, local = bf(bsz, t, d), bf(bsz, t, d), (0.3 * bf(bsz, 6 * d)).to(torch.bfloat16), bf(d), bf(d)
+    kw = dict(y=y, weight=w, eps=1e-6)
+    if mods in ("all", "gate_only"):
+        kw["gate"] = cond[:, 2 * d:3 * d]
+    if mods == "all":
+        kw.update(scale=cond[:, :d], shift=cond[:, d:2 * d], local=local, local_row0=8)
+    h1, h2 = h0.clone(), h0.clone()
+    x = dit_glue.residual_norm(h1, **kw)
+    q, s = dit_glue.residual_norm(h2, quantize=True, **kw)
+    q_ref, s_ref = quantize_rows(x.reshape(-1, d))
+    torch.cuda.synchronize()
+    assert torch.equal(h1, h2)
+    assert torch.equal(q, q_ref) and torch.equal(s, s_ref)
