@@ -28,6 +28,10 @@ class DiTConfig:
     attention: Literal["xla", "fused", "cuda"] = "cuda"
     fused_min_tokens: int = 0  # the reference gates its TPU kernel at 800 tokens; the B200 kernel has no floor
     ff_quant: Literal["none", "w8a8"] = "none"
+    # "w8a8": the self-attention's `to_qkv` as a W8A8 GEMM fed by the pre-norm kernel's per-token int8 output
+    # (glue="cuda", one rank per batch group); `to_out` stays bf16 (its input would need a quantiser pass of its
+    # own, which costs more than the int8 GEMM saves at d = 1024)
+    qkv_quant: Literal["none", "w8a8"] = "none"
     full_head_rope: bool = False  # True: rotate all 64 dims (the benchmark configs); False: the reference's 32
 
     @property

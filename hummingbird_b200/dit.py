@@ -106,6 +106,8 @@ class DiT:
         self.seq = cfg.num_memory_tokens + shape.latents
         self.t0, self.t1 = par.shard_tokens(self.seq, self.world, self.rank)
         self.mem_rows = max(0, min(self.t1, cfg.num_memory_tokens) - self.t0)
+        if cfg.qkv_quant == "w8a8" and (self.world > 1 or glue != "cuda"):
+            raise ValueError("qkv_quant='w8a8' needs glue='cuda' and one rank per batch group")
         if (cfg.num_heads // 2) % self.world or self.t1 - self.t0 <= self.mem_rows:
             raise ValueError(f"a clip of {self.seq} tokens and {cfg.num_heads // 2} head pairs does not split "
                              f"over {self.world} ranks (equal pair counts, latent rows on every rank)")
@@ -150,6 +152,8 @@ class DiT:
             if self.world > 1:  # rows grouped by destination rank: one batched GEMM fills the all-to-all buffer
                 rows = par.dest_major_qkv_rows(h, self.world).to(device)
                 b["self_attn"]["to_qkv_dest"] = b["self_attn"]["to_qkv"][rows].view(self.world, -1, d).transpose(1, 2)
+            if cfg.qkv_quant == "w8a8":
+                b["self_attn"]["to_qkv_q"] = W8A8Linear(b["self_attn"]["to_qkv"])
             if cfg.ff_quant == "w8a8":
                 b["glu_q"] = W8A8Linear(b["glu"]["w"], b["glu"]["b"])
                 b["glu_fused"] = W8A8GluLinear(b["glu"]["w"], b["glu"]["b"])
@@ -267,11 +271,13 @@ class DiT:
         def part(c, i):  # scale_self, shift_self, gate_self, scale_ff, shift_ff, gate_ff (dit.py:230-232)
             return c[:, i * d:(i + 1) * d]
 
+        qkv_q = cfg.qkv_quant == "w8a8"  # x before the self-attention comes per-token quantised, for to_qkv
         c0 = conds[0]
-        x = glue.residual_norm(h, weight=self.blocks[0]["pre_norm_bf"], scale=part(c0, 0), shift=part(c0, 1), eps=eps)
+        x = glue.residual_norm(h, weight=self.blocks[0]["pre_norm_bf"], scale=part(c0, 0), shift=part(c0, 1), eps=eps,
+                               quantize=qkv_q)
         for i, b in enumerate(self.blocks):
             c = conds[i]
-            y = self._self_attn(x, b["self_attn"], static) @ b["self_attn"]["to_out"].T
+            y = self._self_attn(x, b["self_attn"], static, lead=h.shape[:-1]) @ b["self_attn"]["to_out"].T
             x = glue.residual_norm(h, y=y, gate=part(c, 2), weight=b["cross_attend_norm_bf"], eps=eps)
             y = self._cross_fused(x, b["cross_attn"], static["cross_kv_rows"][i])
             if self.cfg.ff_quant == "w8a8":  # the MLP's input leaves the norm kernel already quantised per token
@@ -286,17 +292,22 @@ class DiT:
             if i + 1 < len(self.blocks):
                 nb, nc = self.blocks[i + 1], conds[i + 1]
                 x = glue.residual_norm(h, y=y, gate=part(c, 5), weight=nb["pre_norm_bf"], scale=part(nc, 0),
-                                       shift=part(nc, 1), eps=eps)
+                                       shift=part(nc, 1), eps=eps, quantize=qkv_q)
             else:
                 glue.residual_norm(h, y=y, gate=part(c, 5), eps=eps)
         return h
 
-    def _self_attn(self, x, sa, static):
+    def _self_attn(self, x, sa, static, lead=None):
         """`to_qkv` -> fused differential attention (dit.py:185-200), before `to_out`. Over N ranks: this
         rank's rows of every rank's `to_qkv` columns in one batched GEMM, all-to-all to head pairs, the kernel
-        on this rank's pairs over all rows, all-to-all back to this rank's rows."""
+        on this rank's pairs over all rows, all-to-all back to this rank's rows. `x` may be the per-token int8
+        form `(q, scale)` (`qkv_quant="w8a8"`), with `lead` its `(B, T)`."""
         cfg = self.cfg
         args = (sa["q_norm"], sa["k_norm"], static["lane_cos"], static["lane_sin"], static["lane_mask"])
+        if isinstance(x, tuple):
+            lin = sa["to_qkv_q"]
+            qkv = w8a8_gemm(x[0], x[1], lin.qw, lin.sw).view(*lead, -1)
+            return self.attend(qkv, *args, cfg.num_heads, cfg.head_dim, cfg.rope_dim // 2, cfg.qk_norm_eps)
         if self.world == 1:
             return self.attend(x @ sa["to_qkv"].T, *args, cfg.num_heads, cfg.head_dim, cfg.rope_dim // 2,
                                cfg.qk_norm_eps)
