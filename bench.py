@@ -36,7 +36,7 @@ WINDOW = 128
 L_PER_GPU = 82_688
 HEADS = 8
 # DRAM bytes per launch of band_fused_kernel on this workload, from the committed ncu capture (None until taken)
-BAND_NCU_TRAFFIC = 506_679_296
+BAND_NCU_TRAFFIC = 506_192_128
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 
