@@ -28,8 +28,6 @@
 // This file is compiled without relocatable device code (whole-program; see build.py): with -rdc ptxas
 // ignores setmaxnreg. Its kernel records errors in its own status word (band_fused_take_status).
 #define HB_WHOLE_PROGRAM 1
-// One in eight key pairs' exponentials on the FMA pipe (measured best for this kernel; the others use 1 in 4).
-#define HB_POLY_MASK 7
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
