@@ -33,6 +33,8 @@ SIGNATURES: dict[str, list] = {
     "hb_band_workspace_bytes": [_i, _i, _i, _i, _i, C.POINTER(_sz)],
     "hb_band_diff_attn": [_p, _i64, _p, _p, _p, _i, _p, _p, _i64, _i, _i, _i, _i, _i64, _i, _i, _i, _i, _i, _p, _sz,
                           _i, _p],
+    "hb_band_qkv_project": [_p, _i64, _p, _p, _i64, _p, _p, _p, _i, _p, _i64, _i, _i, _i64, _i, _i, _i, _i, _p],
+    "hb_band_diff_attn_prepared": [_p, _i64, _p, _p, _i64, _i, _i, _i, _i, _i, _i, _i, _i, _i, _p],
     "hb_quant_rows_int8": [_p, _i64, _i, _i, _p, _i64, _p, _p],
     "hb_w8a8_gemm": [_p, _i64, _p, _p, _i64, _p, _p, _p, _i64, _p, _i64, _i, _i, _i, _p],
     "hb_w8a8_gemm_glu": [_p, _i64, _p, _p, _i64, _p, _p, _p, _i64, _i, _i, _i, _p],

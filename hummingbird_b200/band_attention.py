@@ -7,6 +7,11 @@ branches); its Pallas tiling knobs (`rows`, `halo`, `sub`, `stack`, `interpret`)
 the sm_100a kernel tiles by 128 rows and walks only the key tiles inside the band. `ValueError` on
 unsupported shapes, as the reference. Additions: `lam` (per-pair lambda; None = 1) and the sequence-shard
 form `band_attention_shard` used with a halo exchange.
+
+The front end of `same_l._attention` (same_l.py:151-161) runs as one GEMM here: `qkv_project` computes
+`_linear(x, to_qkv)` (with `_block`'s DyT pre-norm on x when given, same_l.py:191) and, with `prepare`, the
+q/k DyT + RoPE of the band kernel in its epilogue; `band_attention_prepared` then runs the band kernel without
+its preparation stage. `same_l_attention_x` is the two together: x `(B, S, d)` -> band output `(B, S, H 64)`.
 """
 from __future__ import annotations
 
@@ -75,6 +80,91 @@ def band_attention(qkv: torch.Tensor, q_norm, k_norm, inv_freq: torch.Tensor, nu
     length = qkv.shape[1]
     return band_attention_shard(qkv, q_norm, k_norm, inv_freq, num_heads, head_dim, window, q_begin=0,
                                 q_count=length, pos0=0, lam=lam, out=out, ws=ws)
+
+
+def pack_pre_norm(norm: dict, d_model: int, device: torch.device) -> torch.Tensor:
+    """The block's DyT `{"alpha": scalar, "gamma": (d,), "beta": (d,)}` -> fp32 `[alpha, gamma[d], beta[d]]`."""
+    alpha = torch.as_tensor(norm["alpha"], dtype=torch.float32, device=device).reshape(-1)[:1]
+    gamma = torch.as_tensor(norm["gamma"], dtype=torch.float32, device=device).reshape(-1)
+    beta = torch.as_tensor(norm["beta"], dtype=torch.float32, device=device).reshape(-1)
+    if gamma.numel() != d_model or beta.numel() != d_model:
+        raise ValueError(f"pre-norm gamma / beta must have d_model = {d_model} entries")
+    return torch.cat([alpha, gamma, beta]).contiguous()
+
+
+def qkv_project(x: torch.Tensor, to_qkv: torch.Tensor, q_norm, k_norm, inv_freq: torch.Tensor, num_heads: int,
+                *, pre_norm=None, prepare: bool = True, pos0: int = 0,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+    """`(B, S, d)` bf16 -> `(B, S, 5 H 64)` bf16: `_linear(x', to_qkv)` (same_l.py:157) with
+    `x' = bf16(DyT(x, pre_norm))` when `pre_norm` is given (same_l.py:191), else x. With `prepare`, the q, k,
+    q_diff, k_diff columns leave DyT'd and rotated (buffer row r at position `pos0 + r`), ready for
+    `band_attention_prepared`. `to_qkv` is the checkpoint's `[5 H 64, d]` weight; d <= 512."""
+    if x.dim() != 3 or x.dtype != torch.bfloat16:
+        raise ValueError(f"x must be bf16 (B, S, d), got {tuple(x.shape)} {x.dtype}")
+    check_cuda(x)
+    batch, rows, d = x.shape
+    n = 5 * num_heads * 64
+    if to_qkv.dtype != torch.bfloat16 or tuple(to_qkv.shape) != (n, d):
+        raise ValueError(f"to_qkv must be bf16 ({n}, {d}), got {tuple(to_qkv.shape)} {to_qkv.dtype}")
+    x = x if x.stride(-1) == 1 and x.stride(0) == x.stride(1) * rows else x.contiguous()
+    w = to_qkv if to_qkv.stride(-1) == 1 else to_qkv.contiguous()
+    pre = None
+    if pre_norm is not None:
+        pre = pre_norm if isinstance(pre_norm, torch.Tensor) else pack_pre_norm(pre_norm, d, x.device)
+    qn = kn = freqs = None
+    half = 0
+    if prepare:
+        qn = q_norm if isinstance(q_norm, torch.Tensor) else pack_norm(q_norm, x.device)
+        kn = k_norm if isinstance(k_norm, torch.Tensor) else pack_norm(k_norm, x.device)
+        freqs = inv_freq.to(device=x.device, dtype=torch.float32).contiguous()
+        half = freqs.shape[0]
+    if out is None:
+        out = torch.empty(batch, rows, n, dtype=torch.bfloat16, device=x.device)
+    if out.stride(-1) != 1 or out.stride(0) != out.stride(1) * rows:
+        raise ValueError("out must have unit column stride and consecutive rows across the batch")
+    _lib.call("hb_band_qkv_project", ptr(x), x.stride(1), ptr(pre), ptr(w), w.stride(0), ptr(qn), ptr(kn), ptr(freqs),
+              half, ptr(out), out.stride(1), batch, rows, pos0, d, num_heads, 64, 1 if prepare else 0,
+              stream_handle(x.device))
+    return out
+
+
+def band_attention_prepared(qkv: torch.Tensor, num_heads: int, window: int, *, q_begin: int = 0,
+                            q_count: int | None = None, lam: torch.Tensor | None = None, pair_begin: int = 0,
+                            pair_count: int | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """`band_attention_shard` on the output of `qkv_project(..., prepare=True)`: the same result as the raw
+    projection through `band_attention_shard`, without the preparation stage. Window <= 128."""
+    if qkv.dim() != 3 or qkv.dtype != torch.bfloat16 or qkv.shape[-1] != 5 * num_heads * 64:
+        raise ValueError(f"qkv must be bf16 (B, S, 5 * H * 64), got {tuple(qkv.shape)} {qkv.dtype}")
+    check_cuda(qkv)
+    batch, rows, _ = qkv.shape
+    q_count = rows - q_begin if q_count is None else q_count
+    pair_count = num_heads // 2 - pair_begin if pair_count is None else pair_count
+    qkv = qkv if qkv.stride(-1) == 1 and qkv.stride(0) == qkv.stride(1) * rows else qkv.contiguous()
+    if lam is not None:
+        lam = lam.to(device=qkv.device, dtype=torch.float32).contiguous()
+    if out is None:
+        out = torch.empty(batch, q_count, 2 * pair_count * 64, dtype=torch.bfloat16, device=qkv.device)
+    _lib.call("hb_band_diff_attn_prepared", ptr(qkv), qkv.stride(1), ptr(lam), ptr(out), out.stride(1), batch, rows,
+              q_begin, q_count, num_heads, 64, window, pair_begin, pair_count, stream_handle(qkv.device))
+    return out
+
+
+def fused_front_end_ok(d_model: int, window: int) -> bool:
+    """Whether `same_l_attention_x` takes the one-GEMM front end (d_model <= 512, window <= 128)."""
+    return d_model % 64 == 0 and 64 <= d_model <= 512 and 0 <= window <= 128
+
+
+def same_l_attention_x(x: torch.Tensor, to_qkv: torch.Tensor, q_norm, k_norm, inv_freq: torch.Tensor,
+                       num_heads: int, window: int, *, pre_norm=None, lam: torch.Tensor | None = None,
+                       qkv: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """`same_l._attention` up to `to_out` (same_l.py:151-161): x `(B, S, d)` -> `(B, S, H 64)`, through the
+    one-GEMM front end and the band kernel without its preparation stage (`qkv` is an optional `(B, S, 5 H 64)`
+    buffer for the prepared projection)."""
+    if not fused_front_end_ok(x.shape[-1], window):
+        raise ValueError(f"same_l_attention_x: needs d_model a multiple of 64 in [64, 512] and window <= 128 "
+                         f"(d_model={x.shape[-1]}, window={window})")
+    qkv = qkv_project(x, to_qkv, q_norm, k_norm, inv_freq, num_heads, pre_norm=pre_norm, prepare=True, out=qkv)
+    return band_attention_prepared(qkv, num_heads, window, lam=lam, out=out)
 
 
 _STREAMS: dict[int, tuple] = {}

@@ -24,7 +24,7 @@ SOURCES = ["abi.cu", "attn_kernel.cu", "attn_dense.cu", "dense_attn.cu", "band_a
            "dit_glue.cu"]
 # Compiled as whole-program device code (no -rdc) into an object linked into the same library: ptxas ignores
 # setmaxnreg in relocatable device code, and these kernels rebalance registers between warpgroups with it.
-WHOLE_PROGRAM_SOURCES = ["band_fused.cu"]
+WHOLE_PROGRAM_SOURCES = ["band_fused.cu", "band_proj.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

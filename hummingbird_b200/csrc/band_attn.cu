@@ -186,3 +186,44 @@ extern "C" int hb_band_diff_attn(const void* qkv, int64_t qkv_row_stride, const 
   ap.out_row_stride = out_row_stride;
   return launch_diff_attention(ap, stream) == cudaSuccess ? HB_OK : HB_ERR_LAUNCH;
 }
+
+// The band attention on qkv that hb_band_qkv_project already prepared (q, k, q_diff, k_diff DyT'd and rotated,
+// rounded to bf16): the fused kernel with its preparation stage skipped. Window <= 128 only.
+extern "C" int hb_band_diff_attn_prepared(const void* qkv, int64_t qkv_row_stride, const float* lam, void* out,
+                                          int64_t out_row_stride, int batch, int rows, int q_begin, int q_count,
+                                          int num_heads, int head_dim, int window, int pair_begin, int pair_count,
+                                          cudaStream_t stream) {
+  if (!qkv || !out) return HB_ERR_NULL;
+  if (head_dim != kHeadDim || num_heads < 2 || num_heads % 2 || batch < 1 || rows < 1 || window < 0 ||
+      window > kFusedMaxWindow)
+    return HB_ERR_SHAPE;
+  if (q_begin < 0 || q_count < 1 || q_begin + q_count > rows) return HB_ERR_SHAPE;
+  if (pair_begin < 0 || pair_count < 1 || pair_begin + pair_count > num_heads / 2) return HB_ERR_SHAPE;
+  if (qkv_row_stride < (int64_t)5 * num_heads * kHeadDim || out_row_stride < (int64_t)2 * pair_count * kHeadDim)
+    return HB_ERR_SHAPE;
+  if (!aligned16(qkv) || qkv_row_stride % 8 || !aligned16(out) || out_row_stride % 8) return HB_ERR_ALIGN;
+  int st = check_device();
+  if (st != HB_OK) return st;
+  BandFusedParams fp{};
+  fp.qkv = static_cast<const uint16_t*>(qkv);
+  fp.row_stride = qkv_row_stride;
+  fp.B = batch;
+  fp.rows = rows;
+  fp.H_total = num_heads;
+  fp.head0 = 2 * pair_begin;
+  fp.heads = 2 * pair_count;
+  fp.q_begin = q_begin;
+  fp.q_count = q_count;
+  fp.window = window;
+  fp.half = 8;
+  fp.lam = lam;
+  fp.lam_pair0 = pair_begin;
+  fp.out = static_cast<uint16_t*>(out);
+  fp.out_row_stride = out_row_stride;
+  fp.qt_first = q_begin / kTileRows;
+  fp.nqt = (q_begin + q_count - 1) / kTileRows - fp.qt_first + 1;
+  fp.ntiles = (rows + kTileRows - 1) / kTileRows;
+  fp.units = batch * fp.heads * fp.nqt;
+  fp.prepared = 1;
+  return band_fused_attend(fp, stream);
+}

@@ -22,6 +22,10 @@
 // tile (of this unit or the next) is computed while it works; P is written once the previous P V has read
 // it. O is single-buffered: the epilogue warps load it and release it before the next unit's first P V.
 //
+// Prepared input (BandFusedParams::prepared, from hb_band_qkv_project): the tiles arrive already DyT'd, rotated
+// and rounded to bf16, so the MMA thread waits on the TMA barriers directly and the preparation warps only run
+// the epilogues (warps 12-15).
+//
 // MMA order over the CTA's flat list of key tiles t: S_A(0), S_B(0); then for each t: S_A(t+1), S_B(t+1),
 // PV_A(t), PV_B(t). A key tile's ring slot is released after the last P V that reads it.
 //
@@ -64,9 +68,6 @@ constexpr int kOffScale = kOffNorm + 2 * kNormStride * 4;  // [2 units][2 branch
 constexpr int kOffFreq = kOffScale + 2 * 2 * kTileRows * 4;
 constexpr int kSmemBytes = kOffFreq + 32 * 4 + 1024;
 constexpr uint32_t kColS = 0, kColP = 256, kColO = 384;
-// 2 pi = kTwoPi1 + kTwoPi2 + kTwoPi3 (fp32 parts of 2 pi taken to 60 digits) and fp32(1 / (2 pi))
-constexpr float kTwoPi1 = 6.2831854820251465f, kTwoPi2 = -1.7484555314695172e-07f, kTwoPi3 = -6.8604980400235275e-15f;
-constexpr float kInvTwoPi = 0.15915493667125702f;
 constexpr float kScoreScale = 1.4426950408889634f * 0.125f;
 constexpr float kRescaleThreshold = 8.0f;
 
@@ -161,18 +162,6 @@ __device__ __forceinline__ bool slack_wait(uint64_t* bar, uint32_t parity) {
 __device__ __forceinline__ bool warp_slack_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
   const bool ok = slack_wait(bar, parity) && !*abort_flag;
   return __all_sync(0xffffffffu, ok);
-}
-
-// cos / sin of an fp32 angle: Cody-Waite reduction by 2 pi (three-part constant, FMA) to |r| <= ~pi, then
-// the hardware approximations on the reduced argument (absolute error ~2^-21 there).
-__device__ __forceinline__ void sincos_reduced(float x, float& sn, float& cs) {
-  // k = rint(x / 2 pi) by adding and subtracting 1.5 * 2^23 (exact for |x / 2 pi| < 2^22), on the FMA pipe
-  const float k = __fadd_rn(__fmaf_rn(x, kInvTwoPi, 12582912.0f), -12582912.0f);
-  float r = fmaf(-k, kTwoPi1, x);
-  r = fmaf(-k, kTwoPi2, r);
-  r = fmaf(-k, kTwoPi3, r);
-  sn = __sinf(r);
-  cs = __cosf(r);
 }
 
 // Eight consecutive fp32 values of shared memory, read at the point of use (kept out of registers across
@@ -320,9 +309,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   for (int i = threadIdx.x; i < 2 * kNormStride; i += kThreads) {
     const int which = i / kNormStride, k = i - which * kNormStride;
-    norms[i] = (k >= 3 && k < 132) ? (which ? p.k_norm : p.q_norm)[k - 3] : 0.f;
+    norms[i] = (!p.prepared && k >= 3 && k < 132) ? (which ? p.k_norm : p.q_norm)[k - 3] : 0.f;
   }
-  if (threadIdx.x < 32) freqs[threadIdx.x] = threadIdx.x < p.half ? p.inv_freq[threadIdx.x] : 0.f;
+  if (threadIdx.x < 32) freqs[threadIdx.x] = (!p.prepared && threadIdx.x < p.half) ? p.inv_freq[threadIdx.x] : 0.f;
   if (warp == 1) {
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
@@ -382,6 +371,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t idS = idesc_bf16_f32(128, 128, false);
       constexpr uint32_t idO = idesc_bf16_f32(128, 64, true);
       const uint32_t qbase = smem_u32(smem + kOffQ), kbase = smem_u32(smem);
+      // prepared input: the MMA reads the tiles as they land (no preparation stage in between)
+      uint64_t* const q_ready = p.prepared ? q_raw : q_full;
+      uint64_t* const k_ready = p.prepared ? k_raw : k_full;
       // Key tile t of the flat list: its unit, ring slot, place in the unit and whether its slot is released
       // after its P V (no later unit of this run reads the same key tile).
       struct Tile {
@@ -412,13 +404,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         tl.rel = !(j + 1 < nunits && same_run(cur, nx) && kt >= nx.klo);
         // a key tile not loaded before this unit waits for its preparation
         if (kt >= sch.first_new) {
-          if (!mma_wait(&k_full[tl.slot], (s / kSlots) & 1) || *abort_flag) ok = false;
+          if (!mma_wait(&k_ready[tl.slot], (s / kSlots) & 1) || *abort_flag) ok = false;
         }
         ++kt;
         return true;
       };
       auto issue_s = [&](const Tile& tl, int t) {
-        if (tl.first && (!mma_wait(&q_full[tl.qb], (tl.j >> 1) & 1) || *abort_flag)) {
+        if (tl.first && (!mma_wait(&q_ready[tl.qb], (tl.j >> 1) & 1) || *abort_flag)) {
           ok = false;
           return;
         }
@@ -641,9 +633,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     };
+    int nunits_prep = nunits;
+    if (p.prepared) {  // nothing to prepare: warps 12-15 run the epilogues, warps 2-3 are idle
+      for (int j = 0; ok && epi && j < nunits; ++j) epilogue(j);
+      nunits_prep = 0;
+    }
     Sched sch;
 #pragma unroll 1
-    for (int j = 0; ok && j < nunits; ++j) {
+    for (int j = 0; ok && j < nunits_prep; ++j) {
       const Unit x = decode(p, u0 + j);
       sch.advance(x, p.heads);
       // the unit's q tile, then its new key tiles; then (warps 12-15) the epilogue of the previous unit
@@ -666,7 +663,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (ok && epi && j > 0) epilogue(j - 1);
     }
-    if (ok && epi && nunits > 0) epilogue(nunits - 1);
+    if (ok && epi && nunits_prep > 0) epilogue(nunits_prep - 1);
   }
   tc_fence_before();
   __syncthreads();

@@ -20,6 +20,7 @@ struct BandFusedParams {
   uint16_t* out;
   int64_t out_row_stride;
   int qt_first, nqt, ntiles, units;
+  int prepared;             // qkv already DyT'd and rotated (hb_band_qkv_project): no preparation stage
 };
 
 constexpr int kFusedMaxWindow = 128;

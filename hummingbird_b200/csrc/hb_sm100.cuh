@@ -303,6 +303,37 @@ __device__ __forceinline__ void mma_i8_ss_pair(uint32_t d_tmem, uint64_t a_desc,
       "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}"
       ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate) : "memory");
 }
+// Pair MMA with A from TMEM (each CTA's TMEM holds its M / 2 rows at the same address), kind::f16.
+__device__ __forceinline__ void mma_bf16_ts_pair(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                                 uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+      ::"r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate) : "memory");
+}
+// Bounded wait with cluster-scope acquire, for a barrier that the peer CTA of a pair arrives on (its writes
+// before its release-arrive are visible after this returns true).
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, unsigned int code = HB_ERR_TIMEOUT) {
+  auto try_once = [&]() {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.b32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+    return ok != 0;
+  };
+  if (try_once()) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+    for (int i = 0; i < 64; ++i)
+      if (try_once()) return true;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      record_error(code);
+      return false;
+    }
+  }
+}
 // Arrive on `cluster_bar` (either CTA of the pair) once the pair MMAs issued so far have completed.
 __device__ __forceinline__ void tc_commit_pair(uint32_t cluster_bar) {
   asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(cluster_bar)

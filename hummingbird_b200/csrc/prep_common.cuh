@@ -34,4 +34,20 @@ __device__ __forceinline__ uint4 ld_nc_v4(const void* p) {
 // dims [0, half) pair with d + half, the rest with d - half (band_attention.py:77, 84).
 __device__ __forceinline__ int rope_partner_chunk(int c, int hc8) { return c < hc8 ? c + hc8 : c - hc8; }
 
+// 2 pi = kTwoPi1 + kTwoPi2 + kTwoPi3 (fp32 parts of 2 pi taken to 60 digits) and fp32(1 / (2 pi))
+constexpr float kTwoPi1 = 6.2831854820251465f, kTwoPi2 = -1.7484555314695172e-07f, kTwoPi3 = -6.8604980400235275e-15f;
+constexpr float kInvTwoPi = 0.15915493667125702f;
+
+// cos / sin of an fp32 angle: Cody-Waite reduction by 2 pi (three-part constant, FMA) to |r| <= ~pi, then
+// the hardware approximations on the reduced argument (absolute error ~2^-21 there).
+__device__ __forceinline__ void sincos_reduced(float x, float& sn, float& cs) {
+  // k = rint(x / 2 pi) by adding and subtracting 1.5 * 2^23 (exact for |x / 2 pi| < 2^22), on the FMA pipe
+  const float k = __fadd_rn(__fmaf_rn(x, kInvTwoPi, 12582912.0f), -12582912.0f);
+  float r = fmaf(-k, kTwoPi1, x);
+  r = fmaf(-k, kTwoPi2, r);
+  r = fmaf(-k, kTwoPi3, r);
+  sn = __sinf(r);
+  cs = __cosf(r);
+}
+
 }  // namespace hb

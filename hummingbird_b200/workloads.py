@@ -9,6 +9,9 @@ kernel input `qkv = bf16(x @ W_qkv^T)` is shared bit for bit by the GPU path and
 * band (config 2): B=1, L=82,688, d=512, 8 heads, window 128, DyT alpha 0.5, gamma 1 + N(0, 0.02),
   beta N(0, 0.02), RoPE base 1e4 on the first 32 dims (half 16, the SAME-L reference's
   `RotaryEmbedding(dim_heads // 2)`, same_l.py:84-89), lambda ~ U(0.2, 0.8), seed 1.
+* band layer (config 2 through the front end): the same shapes with x ~ N(0, 1) rounded to bf16 as the
+  layer's input, to_qkv ~ N(0, 1/d) rounded to bf16, and the block's DyT pre-norm (alpha 0.5, gamma
+  1 + N(0, 0.02), beta N(0, 0.02) over d), seed 11.
 * w8a8 (config 3): M=2,584; x ~ N(0,1) bf16; W1 (4096, 1024) ~ N(0, 1/1024); W2 (1024, 4096) ~ N(0, 1/4096);
   biases N(0, 0.02); seed 3.
 """
@@ -93,6 +96,38 @@ def band_inputs(device, *, seed=1, batch=1, length=82_688, d_model=512, heads=8,
     lam = rng.uniform(0.2, 0.8, heads // 2).astype(np.float32)
     qkv = _project(x, w, device).reshape(batch, length, 5 * heads * 64)
     return BandInputs(qkv, qn, kn, inv_freq(half), lam, heads, window)
+
+
+@dataclass
+class BandLayerInputs:
+    x: torch.Tensor            # (B, L, d) bf16: the block input before its DyT pre-norm
+    to_qkv: torch.Tensor       # (5 H 64, d) bf16, the checkpoint's [out, in]
+    pre_norm: dict             # block DyT {"alpha", "gamma" (d,), "beta" (d,)}
+    q_norm: dict
+    k_norm: dict
+    inv_freq: np.ndarray
+    lam: np.ndarray
+    heads: int
+    window: int
+
+
+def band_layer_inputs(device, *, seed=11, batch=1, length=82_688, d_model=512, heads=8, half=16, window=128):
+    """The SAME-L attention layer's own inputs (x and the to_qkv weight) for the one-GEMM front end."""
+    rng = np.random.default_rng(seed)
+    bf = lambda a: torch.from_numpy(np.asarray(a, np.float32)).to(device).to(torch.bfloat16)  # noqa: E731
+    x = bf(rng.standard_normal((batch, length, d_model), dtype=np.float32))
+    w = bf(np.concatenate([rng.standard_normal((heads * 64, d_model), dtype=np.float32) / np.sqrt(d_model)
+                           for _ in range(5)]))
+    pre = {"alpha": np.float32(0.5), "gamma": (1.0 + 0.02 * rng.standard_normal(d_model)).astype(np.float32),
+           "beta": (0.02 * rng.standard_normal(d_model)).astype(np.float32)}
+
+    def norm():
+        return {"alpha": np.float32(0.5), "gamma": (1.0 + 0.02 * rng.standard_normal(64)).astype(np.float32),
+                "beta": (0.02 * rng.standard_normal(64)).astype(np.float32)}
+
+    qn, kn = norm(), norm()
+    lam = rng.uniform(0.2, 0.8, heads // 2).astype(np.float32)
+    return BandLayerInputs(x, w, pre, qn, kn, inv_freq(half), lam, heads, window)
 
 
 @dataclass

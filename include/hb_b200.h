@@ -132,6 +132,30 @@ int hb_band_diff_attn(const void* qkv, int64_t qkv_row_stride, const float* q_no
                       int window, int pair_begin, int pair_count, void* workspace, size_t workspace_bytes,
                       int stages, cudaStream_t stream);
 
+/* The SAME-L attention front end in one GEMM (same_l.py:157-160, 191): qkv = bf16(x' to_qkv^T) with
+ * x' = bf16(DyT(x, pre_norm)) when pre_norm is given (`_block`'s `_dyt(x, pre_norm).astype(compute)`), x otherwise.
+ *   x         bf16 [batch, rows, d_model] (row stride ldx elements); 64 <= d_model <= 512, a multiple of 64.
+ *   pre_norm  fp32 [1 + 2 d_model] {alpha, gamma[d_model], beta[d_model]} or NULL.
+ *   w         bf16 [5 * num_heads * 64, d_model] (row stride ldw): the checkpoint's `to_qkv` weight [out, in].
+ *   out       bf16 [batch, rows, ldo], columns [q | k | v | q_diff | k_diff] as hb_band_diff_attn reads them.
+ *   prepare   0: out is the projection. 1: the q, k, q_diff, k_diff columns are DyT'd (q_norm / k_norm, fp32
+ *             [129]) and rotated (RoPE, inv_freq fp32 [half], angles fp32(pos0 + row) * inv_freq) in fp32 and
+ *             rounded to bf16 once, with the fused band kernel's arithmetic: hb_band_diff_attn_prepared on this
+ *             output equals hb_band_diff_attn on the prepare = 0 output bit for bit (window <= 128).
+ * No reference counterpart as one entry point: the reference runs the projection as an XLA matmul and the
+ * DyT / RoPE inside its Pallas kernel. */
+int hb_band_qkv_project(const void* x, int64_t ldx, const float* pre_norm, const void* w, int64_t ldw,
+                        const float* q_norm, const float* k_norm, const float* inv_freq, int half, void* out,
+                        int64_t ldo, int batch, int rows, int64_t pos0, int d_model, int num_heads, int head_dim,
+                        int prepare, cudaStream_t stream);
+
+/* hb_band_diff_attn on qkv that hb_band_qkv_project prepared (prepare = 1; halo rows from neighbouring shards
+ * prepared at their own positions): the fused kernel without its preparation stage. Arguments as for
+ * hb_band_diff_attn; window <= 128. */
+int hb_band_diff_attn_prepared(const void* qkv, int64_t qkv_row_stride, const float* lam, void* out,
+                               int64_t out_row_stride, int batch, int rows, int q_begin, int q_count, int num_heads,
+                               int head_dim, int window, int pair_begin, int pair_count, cudaStream_t stream);
+
 /* ---- W8A8 int8 GEMM (DiT MLP) ------------------------------------------------------------------------ */
 /* Per-row symmetric int8 quantisation of a bf16 matrix x [rows, K] (leading dim ldx elements):
  * scale[r] = absmax / 127 (1 for an all-zero row), q = clamp(rint(x / scale), -127, 127).

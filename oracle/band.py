@@ -10,6 +10,9 @@ Follows `same_l._attention` (same_l.py:151-169) under `FP32_PARITY`, computed in
   `_windows` form, same_l.py:103-148, is the same function), weights times fp32 `v`
 * `out = A - lambda * B` in fp32 (same_l.py:168; lambda = 1 is the reference).
 
+and the front end of `same_l._attention` as `_block` calls it (`front_end`): the block's DyT pre-norm cast to
+the compute dtype (same_l.py:191), then `_linear(x, to_qkv)` (same_l.py:52-55, 157) rounded to bf16.
+
 Written as a direct band walked in query blocks, so any window and any L work (the grouped XLA form
 needs `L % window == 0`).
 """
@@ -24,6 +27,17 @@ def dyt(x: np.ndarray, norm: dict) -> np.ndarray:
     """`DynamicTanh`: `gamma * tanh(alpha * x) + beta`, alpha a scalar (same_l.py:58-69)."""
     alpha = x.dtype.type(np.asarray(norm["alpha"], np.float32).reshape(-1)[0])
     return (np.asarray(norm["gamma"], x.dtype) * np.tanh(alpha * x) + np.asarray(norm["beta"], x.dtype))
+
+
+def front_end(x: np.ndarray, to_qkv: np.ndarray, pre_norm: dict | None = None) -> np.ndarray:
+    """`(B, L, d)` -> `(B, L, 5 H 64)` float64 holding bf16 values: `x' = bf16(dyt(x, pre_norm))` in fp32 when
+    `pre_norm` is given (`_dyt(x, block["pre_norm"]).astype(dtype.compute)`, same_l.py:191), else x; then
+    `bf16(x' @ to_qkv^T)` accumulated in float64 (`_linear`, same_l.py:52-55, 157, in the compute dtype)."""
+    x = np.asarray(x, np.float32)
+    if pre_norm is not None:
+        x = bf16(dyt(x, pre_norm))
+    y = np.matmul(x.astype(np.float64), np.asarray(to_qkv, np.float64).T)
+    return bf16(y.astype(np.float32))
 
 
 def band_attend(q: np.ndarray, k: np.ndarray, v: np.ndarray, window: int, block: int = 256,

@@ -4,6 +4,8 @@
     python profile_cases.py dense   # dense DiT self-attention, B=2, L=2,648, 16 heads
     python profile_cases.py cross   # DiT cross-attention, B=2, 2,648 queries, 128 context, 16 heads
     python profile_cases.py glue    # DiT row kernels: residual + RMSNorm + adaLN, GLU + int8
+    python profile_cases.py band_front [--rows R]  # SAME-L front end (block DyT + to_qkv + q/k DyT + RoPE) and
+                                                   # the band kernel on its output; config 2 at R = 82,688 rows
 
 Each case builds its seeded synthetic inputs (`hummingbird_b200.workloads`), makes `--calls` calls (default 3)
 on the current GPU and prints a checksum of the last output. Nothing is timed here: the bench times.
@@ -72,15 +74,29 @@ def glue(calls: int) -> torch.Tensor:
     return x.float().mean() + q.float().mean()
 
 
-CASES = {"band": band, "dense": dense, "cross": cross, "glue": glue}
+def band_front(calls: int, rows: int = 82_688) -> torch.Tensor:
+    from hummingbird_b200.band_attention import pack_norm, pack_pre_norm, same_l_attention_x
+    from hummingbird_b200.workloads import band_layer_inputs
+    w = band_layer_inputs("cuda", length=rows)
+    lam, freqs = torch.from_numpy(w.lam).cuda(), torch.from_numpy(w.inv_freq).cuda()
+    qn, kn = pack_norm(w.q_norm, "cuda"), pack_norm(w.k_norm, "cuda")
+    pre = pack_pre_norm(w.pre_norm, w.x.shape[-1], "cuda")
+    for _ in range(calls):
+        out = same_l_attention_x(w.x, w.to_qkv, qn, kn, freqs, w.heads, w.window, pre_norm=pre, lam=lam)
+    return out
+
+
+CASES = {"band": band, "dense": dense, "cross": cross, "glue": glue, "band_front": band_front}
 
 
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("case", choices=sorted(CASES))
     ap.add_argument("--calls", type=int, default=3)
+    ap.add_argument("--rows", type=int, default=None, help="sequence rows (band_front only)")
     args = ap.parse_args()
-    out = CASES[args.case](args.calls)
+    kw = {"rows": args.rows} if args.rows and args.case == "band_front" else {}
+    out = CASES[args.case](args.calls, **kw)
     torch.cuda.synchronize()
     print(args.case, "ok", float(out.float().abs().mean()))
 

@@ -129,6 +129,60 @@ def test_band_prepare_stage_needs_no_output(lib):
         _lib.HB_ERR_WORKSPACE
 
 
+def _proj(**kw):
+    """Arguments of a valid config-2 front-end call (x (1, 82,688, 512), to_qkv (2560, 512), prepared), with
+    overrides."""
+    a = dict(x=P, ldx=512, pre=P, w=P, ldw=512, q_norm=P, k_norm=P, inv_freq=P, half=16, out=P, ldo=2560, batch=1,
+             rows=82688, pos0=0, d_model=512, heads=8, head_dim=64, prepare=1, stream=None)
+    a.update(kw)
+    return list(a.values())
+
+
+@pytest.mark.parametrize("override,status", [
+    (dict(d_model=576, ldx=576, ldw=576), _lib.HB_ERR_SHAPE),   # x tile no longer fits in shared memory
+    (dict(d_model=96, ldx=96, ldw=96), _lib.HB_ERR_SHAPE),      # not whole 64-column chunks
+    (dict(heads=7), _lib.HB_ERR_SHAPE),
+    (dict(head_dim=32), _lib.HB_ERR_SHAPE),
+    (dict(half=12), _lib.HB_ERR_SHAPE),
+    (dict(ldo=2552), _lib.HB_ERR_SHAPE),
+    (dict(pos0=(1 << 24) - 82687), _lib.HB_ERR_SHAPE),
+    (dict(x=MIS), _lib.HB_ERR_ALIGN),
+    (dict(ldw=516), _lib.HB_ERR_ALIGN),
+    (dict(x=None), _lib.HB_ERR_NULL),
+    (dict(k_norm=None), _lib.HB_ERR_NULL),
+])
+def test_band_projection_rejects(lib, override, status):
+    assert lib.hb_band_qkv_project(*_proj(**override)) == status
+
+
+def test_band_projection_needs_no_norms_unprepared(lib):
+    # prepare = 0 is the plain projection: the DyT / RoPE parameters may be absent. The null check of the norms
+    # comes before the shape checks, so a call whose only other fault is a short output stride reports the shape
+    # (with prepare = 1 the same call reports the missing norms)
+    kw = dict(q_norm=None, k_norm=None, inv_freq=None, half=0, ldo=2552)
+    assert lib.hb_band_qkv_project(*_proj(prepare=0, **kw)) == _lib.HB_ERR_SHAPE
+    assert lib.hb_band_qkv_project(*_proj(prepare=1, **kw)) == _lib.HB_ERR_NULL
+
+
+def _prepared(**kw):
+    a = dict(qkv=P, qkv_rs=2560, lam=None, out=P, out_rs=512, batch=1, rows=82688, q_begin=0, q_count=82688,
+             heads=8, head_dim=64, window=128, pair_begin=0, pair_count=4, stream=None)
+    a.update(kw)
+    return list(a.values())
+
+
+@pytest.mark.parametrize("override,status", [
+    (dict(window=129), _lib.HB_ERR_SHAPE),        # the prepared form exists for the fused kernel only
+    (dict(q_count=82689), _lib.HB_ERR_SHAPE),
+    (dict(pair_count=5), _lib.HB_ERR_SHAPE),
+    (dict(qkv_rs=2550), _lib.HB_ERR_SHAPE),
+    (dict(out=MIS), _lib.HB_ERR_ALIGN),
+    (dict(qkv=None), _lib.HB_ERR_NULL),
+])
+def test_band_prepared_rejects(lib, override, status):
+    assert lib.hb_band_diff_attn_prepared(*_prepared(**override)) == status
+
+
 def _cross(**kw):
     """Arguments of a valid DiT cross-attention call (B=2, 2,648 queries, 128 context tokens, 16 heads)."""
     a = dict(q=P, q_rs=2048, kv=P, kv_rs=3072, q_w=P, k_w=None, lam=None, out=P, out_rs=1024, batch=2,
