@@ -7,6 +7,10 @@ the hot path over one batch: [halo exchange over NCCL when N > 1] + DyT/RoPE pre
 N > 1 each rank owns an 82,688-row shard of one long sequence (weak scaling) and receives +-128 halo rows
 from its neighbours with NCCL send/recv before its kernels run.
 
+The SAME-L attention layer itself (`e2e_layer`): x -> block DyT pre-norm + to_qkv + q/k DyT + RoPE in one GEMM
+-> the band kernel on the prepared projection -> to_out, device-resident and from pinned host memory, with its
+own CPU baseline (the layer's oracle) and parity check.
+
 Secondary paths (N = 1 only, reported under `paths`): dense DiT differential attention (config 1, and the
 120 s clip's per-block call B=2, L=2,648, 16 heads) and the W8A8 GEMM pair (config 3).
 
@@ -286,6 +290,182 @@ def band_parity(step: BandStep, world: int, edge: int = 384) -> dict:
     return {"ok": all(r[2] == 1.0 for r in allr), "max_abs": max(r[0] for r in allr),
             "mean_abs": max(r[1] for r in allr), "per_rank": [[round(r[0], 5), round(r[1], 6)] for r in allr],
             "rows": f"first and last {edge} own rows per rank vs the fp32 oracle"}
+
+
+# ----------------------------------------------------------------------------------------------- band layer
+LAYER_SEED = 1
+
+
+def band_layer_rank_inputs(device, rank: int):
+    """The SAME-L attention layer's inputs at config 2 (x ~ N(0,1), to_qkv / to_out ~ N(0, 1/512), block DyT
+    pre-norm and q/k DyT alpha 0.5, gamma 1 + N(0, 0.02), beta N(0, 0.02)); ranks > 0 draw other rows of the
+    same sequence with the same weights."""
+    from hummingbird_b200.workloads import band_layer_inputs
+    return band_layer_inputs(device, seed=LAYER_SEED, length=L_PER_GPU, d_model=512, heads=HEADS, window=WINDOW,
+                             x_seed=None if rank == 0 else (LAYER_SEED, rank))
+
+
+class BandLayerStep:
+    """`same_l._attention` of `_block` (same_l.py:151-161, 191) on this rank's 82,688 rows: the one-GEMM front
+    end (block DyT pre-norm + to_qkv + q/k DyT + RoPE, `band_proj_kernel`) on the own rows, [the halo exchange of
+    the prepared rows over NCCL at N > 1], the band kernel on the prepared projection, to_out (cuBLAS)."""
+
+    def __init__(self, device, rank: int, world: int, comm=None):
+        import torch
+        from hummingbird_b200 import band_attention as hb
+        from hummingbird_b200 import parallel as par
+        self.torch, self.hb, self.par = torch, hb, par
+        self.rank, self.world, self.comm = rank, world, comm
+        self.w = band_layer_rank_inputs(device, rank)
+        self.lay = par.band_layout(L_PER_GPU * world, world, rank, WINDOW)
+        self.before = self.lay["before"]
+        self.qkv = torch.zeros(1, self.lay["rows"], 5 * HEADS * 64, dtype=torch.bfloat16, device=device)
+        self.att = torch.empty(1, L_PER_GPU, HEADS * 64, dtype=torch.bfloat16, device=device)
+        self.out = torch.empty_like(self.att)
+        self.qn, self.kn = hb.pack_norm(self.w.q_norm, device), hb.pack_norm(self.w.k_norm, device)
+        self.pre = hb.pack_pre_norm(self.w.pre_norm, 512, device)
+        self.freqs = torch.from_numpy(self.w.inv_freq).to(device)
+        self.lam = torch.from_numpy(self.w.lam).to(device)
+        self.flops = band_flops(L_PER_GPU * world, rank * L_PER_GPU, (rank + 1) * L_PER_GPU)
+        self.proj_flops = 2.0 * L_PER_GPU * 512 * 5 * HEADS * 64
+
+    def project(self):
+        self.hb.qkv_project(self.w.x, self.w.to_qkv, self.qn, self.kn, self.freqs, HEADS, pre_norm=self.pre,
+                            pos0=self.lay["pos0"] + self.before,
+                            out=self.qkv[:, self.before:self.before + L_PER_GPU])
+
+    def exchange(self):
+        if self.world > 1:
+            self.par.halo_exchange(self.qkv, self.lay, self.rank, comm=self.comm)
+
+    def attend(self):
+        self.hb.band_attention_prepared(self.qkv, HEADS, WINDOW, q_begin=self.before, q_count=L_PER_GPU,
+                                        lam=self.lam, out=self.att)
+
+    def to_out(self):
+        self.torch.matmul(self.att[0], self.w.to_out.t(), out=self.out[0])
+
+
+def time_band_layer(step: BandLayerStep, steps: int, warmup: int, world: int) -> dict:
+    """Device-resident layer step (x in HBM): per-stage CUDA events on the launching stream, max over ranks."""
+    import torch
+    stream = torch.cuda.current_stream()
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(steps)]
+    for _ in range(warmup):
+        step.project()
+        step.exchange()
+        step.attend()
+        step.to_out()
+    barrier(world)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for i in range(steps):
+        ev[i][0].record(stream)
+        step.project()
+        ev[i][1].record(stream)
+        step.exchange()
+        step.attend()
+        ev[i][2].record(stream)
+        step.to_out()
+        ev[i][3].record(stream)
+    b.record(stream)
+    barrier(world)
+    proj = statistics.mean(e[0].elapsed_time(e[1]) for e in ev)
+    attn = statistics.mean(e[1].elapsed_time(e[2]) for e in ev)
+    out = statistics.mean(e[2].elapsed_time(e[3]) for e in ev)
+    return {"ms_per_step": max_over_ranks(a.elapsed_time(b) / steps, world), "proj_ms": proj,
+            "attn_ms": attn, "to_out_ms": out}
+
+
+def time_band_layer_e2e(step: BandLayerStep, steps: int, warmup: int, world: int) -> dict:
+    """Through the public API with host buffers (`same_l_attention_from_host`): the layer input x streams from
+    pinned host memory in chunks, is projected on the device (front end), the band kernel and to_out run per
+    chunk, the output streams back to pinned host memory, all inside the timed region. Only x (85 MB) and the
+    output (85 MB) cross PCIe."""
+    import torch
+    x_host = step.w.x.cpu().pin_memory()
+    h_out = torch.empty(step.out.shape, dtype=torch.bfloat16).pin_memory()
+    stream = torch.cuda.current_stream()
+    dev_x = torch.empty_like(step.w.x)
+
+    def one():
+        step.hb.same_l_attention_from_host(x_host, step.w.to_qkv, step.qn, step.kn, step.freqs, HEADS, WINDOW,
+                                           to_out=step.w.to_out, pre_norm=step.pre, lam=step.lam, out_host=h_out,
+                                           dev_x=dev_x, dev_qkv=step.qkv, dev_att=step.att, dev_out=step.out,
+                                           layout=step.lay if world > 1 else None, comm=step.comm)
+
+    for _ in range(warmup):
+        one()
+    barrier(world)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(steps):
+        one()
+    b.record(stream)
+    barrier(world)
+    ms = max_over_ranks(a.elapsed_time(b) / steps, world)
+    return {"ms_per_step": ms, "h2d": x_host.numel() * 2, "d2h": h_out.numel() * 2}
+
+
+def layer_parity(step: BandLayerStep, world: int, edge: int = 384) -> dict:
+    """Output check of the layer step on every rank, outside the timed region: the band output (before to_out)
+    of the first and last `edge` own rows against the oracle run from x (`oracle.band.front_end`: pre-norm +
+    to_qkv; then the band attention), the neighbours' x rows at shard edges regenerated from their seeds.
+    Tolerance max-abs 2e-2, mean-abs 2e-3."""
+    import torch
+    from oracle import band as oband
+    step.project()
+    step.exchange()
+    step.attend()
+    torch.cuda.synchronize()
+    own_x = step.w.x[0].float().cpu().numpy()
+    glob = L_PER_GPU * world
+    g_own = step.rank * L_PER_GPU
+    neighbours = {}
+
+    def x_rows(g0: int, g1: int) -> np.ndarray:
+        parts = []
+        for r in range(g0 // L_PER_GPU, (g1 - 1) // L_PER_GPU + 1):
+            lo, hi = max(g0, r * L_PER_GPU) - r * L_PER_GPU, min(g1, (r + 1) * L_PER_GPU) - r * L_PER_GPU
+            if r == step.rank:
+                parts.append(own_x[lo:hi])
+            else:
+                if r not in neighbours:
+                    neighbours[r] = band_layer_rank_inputs("cpu", r).x[0].float().numpy()
+                parts.append(neighbours[r][lo:hi])
+        return np.concatenate(parts)[None]
+
+    worst, means = 0.0, []
+    for q0 in (0, L_PER_GPU - edge):
+        g0, g1 = max(0, g_own + q0 - WINDOW), min(glob, g_own + q0 + edge + WINDOW)
+        qkv = oband.front_end(x_rows(g0, g1), step.w.to_qkv.float().cpu().numpy(), step.w.pre_norm)
+        ref = oband.band_diff_attention(qkv, step.w.q_norm, step.w.k_norm, step.w.inv_freq, HEADS, WINDOW,
+                                        lam=step.w.lam, offset=g0)
+        a = g_own + q0 - g0
+        got = step.att[:, q0:q0 + edge].float().cpu().numpy()
+        diff = np.abs(got - ref[:, a:a + edge])
+        worst = max(worst, float(diff.max()))
+        means.append(float(diff.mean()))
+    mine = [worst, float(np.mean(means)), float(worst <= 2e-2 and np.mean(means) <= 2e-3)]
+    allr = _gather_rows(mine, world)
+    return {"ok": all(r[2] == 1.0 for r in allr), "max_abs": max(r[0] for r in allr),
+            "mean_abs": max(r[1] for r in allr), "per_rank": [[round(r[0], 5), round(r[1], 6)] for r in allr],
+            "rows": f"first and last {edge} own rows per rank, band output vs the oracle from x"}
+
+
+def cpu_layer_baseline(w, q_rows: int, min_seconds: float = 10.0) -> dict:
+    """The layer's oracle (front end + band + to_out) on the host cores over queries [0, q_rows) of the rank-0
+    workload, repeated until at least `min_seconds` of wall time have been measured."""
+    sys.path.insert(0, str(ROOT))
+    from oracle.cpu_baseline import time_layer_sample
+    rows = min(L_PER_GPU, q_rows + WINDOW)
+    x = w.x[:, :rows].float().cpu().numpy()
+    r = time_layer_sample(x, w.to_qkv.float().cpu().numpy(), w.to_out.float().cpu().numpy(), w.pre_norm, w.q_norm,
+                          w.k_norm, w.inv_freq, HEADS, WINDOW, w.lam, q_rows, min_seconds=min_seconds)
+    return {"value": r["flops"] / r["seconds"] / 1e12, "unit": "TFLOP/s", "cores": r["cores"], "kind": "port",
+            "sample": f"layer (pre-norm + to_qkv, band attention, to_out) over queries 0..{q_rows} of config 2 x "
+                      f"{r['passes']} passes, fp32 numpy oracle, {r['cores']}-process spawn pool, "
+                      f"{r['seconds']:.1f} s; attention FLOPs counted"}
 
 
 # ----------------------------------------------------------------------------------------------- dense
@@ -811,10 +991,13 @@ def main():
         from hummingbird_b200.comm import HbComm
         comm = HbComm(rank, world, timeout_ms=120_000)
     step = BandStep(device, rank, world, comm)
+    layer = BandLayerStep(device, rank, world, comm)
     clocks = ClockSampler(local)
     clocks.start()
     t = time_band(step, args.steps, args.warmup, world)
     e2e = time_band_e2e(step, max(10, args.steps // 4), args.warmup, world)
+    tl = time_band_layer(layer, max(10, args.steps // 2), args.warmup, world)
+    e2e_l = time_band_layer_e2e(layer, max(10, args.steps // 4), args.warmup, world)
     clk = clocks.stop()
     total_flops = sum_over_ranks(step.flops, world)
     value = total_flops / (t["ms_per_step"] * 1e-3) / 1e12
@@ -840,6 +1023,20 @@ def main():
                 "how": "band_attention_from_host: pinned host qkv streamed to the device in 8,192-row chunks, "
                        "halo exchange on the device (N > 1), each chunk's queries as soon as their rows landed, "
                        "output streamed back to pinned host memory"},
+        "e2e_layer": {
+            "value": total_flops / (e2e_l["ms_per_step"] * 1e-3) / 1e12, "unit": "TFLOP/s",
+            "ms_per_step": e2e_l["ms_per_step"], "h2d_bytes_per_step": e2e_l["h2d"],
+            "d2h_bytes_per_step": e2e_l["d2h"],
+            "how": "same_l_attention_from_host: the SAME-L attention layer (same_l._attention of _block: block DyT "
+                   "pre-norm, to_qkv, band attention, to_out) with its input x in pinned host memory, streamed in "
+                   "8,192-row chunks through the one-GEMM front end and the band kernel; attention FLOPs counted",
+            "device_ms_per_step": tl["ms_per_step"],
+            "device_stages_ms": {"front_end": tl["proj_ms"], "band": tl["attn_ms"], "to_out": tl["to_out_ms"]},
+            "front_end_roofline": {"bound": "tensor", "kernel": "band_proj_kernel",
+                                   "achieved": layer.proj_flops / (tl["proj_ms"] * 1e-3) / 1e12,
+                                   "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                                   "frac": layer.proj_flops / (tl["proj_ms"] * 1e-3) / 1e12 / peaks["bf16_tflops"],
+                                   "flops_per_launch": layer.proj_flops}},
         "gpu_launches": step.launches * args.steps,
         "roofline": {"bound": "hbm", "kernel": "band_fused_kernel", "achieved": achieved, "peak": peaks["hbm_gbs"],
                      "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"], "traffic": BAND_NCU_TRAFFIC,
@@ -866,9 +1063,10 @@ def main():
         line["paths"] = paths
     if world == 1 and rank == 0:
         line["cpu_baseline"] = cpu_band_baseline(step.w.qkv, step.w, args.cpu_rows)
+        line["e2e_layer"]["cpu_baseline"] = cpu_layer_baseline(layer.w, args.cpu_rows)
         from oracle.cpu_baseline import shutdown
         shutdown()
-    parity = {"band_headline": band_parity(step, world)}
+    parity = {"band_headline": band_parity(step, world), "band_layer": layer_parity(layer, world)}
     if "paths" in line and line["paths"]["dit_120s_clip_w8a8_mlp"].get("parity"):
         parity["dit_split_step"] = line["paths"]["dit_120s_clip_w8a8_mlp"]["parity"]
     line["parity"] = parity

@@ -106,7 +106,8 @@ def qkv_project(x: torch.Tensor, to_qkv: torch.Tensor, q_norm, k_norm, inv_freq:
     n = 5 * num_heads * 64
     if to_qkv.dtype != torch.bfloat16 or tuple(to_qkv.shape) != (n, d):
         raise ValueError(f"to_qkv must be bf16 ({n}, {d}), got {tuple(to_qkv.shape)} {to_qkv.dtype}")
-    x = x if x.stride(-1) == 1 and x.stride(0) == x.stride(1) * rows else x.contiguous()
+    # rows consecutive across the batch (the batch stride does not matter for one batch element)
+    x = x if x.stride(-1) == 1 and (batch == 1 or x.stride(0) == x.stride(1) * rows) else x.contiguous()
     w = to_qkv if to_qkv.stride(-1) == 1 else to_qkv.contiguous()
     pre = None
     if pre_norm is not None:
@@ -120,7 +121,7 @@ def qkv_project(x: torch.Tensor, to_qkv: torch.Tensor, q_norm, k_norm, inv_freq:
         half = freqs.shape[0]
     if out is None:
         out = torch.empty(batch, rows, n, dtype=torch.bfloat16, device=x.device)
-    if out.stride(-1) != 1 or out.stride(0) != out.stride(1) * rows:
+    if out.stride(-1) != 1 or (batch > 1 and out.stride(0) != out.stride(1) * rows):
         raise ValueError("out must have unit column stride and consecutive rows across the batch")
     _lib.call("hb_band_qkv_project", ptr(x), x.stride(1), ptr(pre), ptr(w), w.stride(0), ptr(qn), ptr(kn), ptr(freqs),
               half, ptr(out), out.stride(1), batch, rows, pos0, d, num_heads, 64, 1 if prepare else 0,
@@ -248,3 +249,106 @@ def band_attention_from_host(qkv_host: torch.Tensor, q_norm, k_norm, inv_freq: t
     main.wait_stream(s_out)
     return out_host
 
+
+
+def same_l_attention_from_host(x_host: torch.Tensor, to_qkv: torch.Tensor, q_norm, k_norm, inv_freq: torch.Tensor,
+                               num_heads: int, window: int, *, to_out: torch.Tensor | None = None, pre_norm=None,
+                               lam: torch.Tensor | None = None, out_host: torch.Tensor | None = None,
+                               dev_x: torch.Tensor | None = None, dev_qkv: torch.Tensor | None = None,
+                               dev_att: torch.Tensor | None = None, dev_out: torch.Tensor | None = None,
+                               layout: dict | None = None, comm=None, chunk_rows: int = 8192) -> torch.Tensor:
+    """`same_l._attention` (same_l.py:151-161) of a layer input held in pinned HOST memory: x `(B, R, d)` bf16
+    streams to the device in chunks; each chunk's rows go through the one-GEMM front end (`qkv_project`,
+    prepared, at their sequence positions); a chunk's queries run through the band kernel once the rows up to
+    `window` past them are projected; with `to_out` (`[H 64, H 64]`, the checkpoint's `[out, in]`) the output
+    projection follows on the chunk; finished rows go back to `out_host` `(B, R, H 64)` (pinned) on a second copy
+    stream. Only x and the output cross PCIe (the projection never does). Returns `out_host`; the current stream
+    is ordered after the last copy back.
+
+    With `layout` (`parallel.band_layout`) and `comm` the rows are this rank's shard of a longer sequence: the
+    rows the neighbours need are projected first and their prepared projections exchanged on the device (the
+    halo rows keep the positions their owner gave them), then the rest streams."""
+    if x_host.is_cuda or x_host.dim() != 3:
+        raise ValueError("x_host must be a (B, R, d) host tensor")
+    device = torch.device("cuda", torch.cuda.current_device())
+    batch, own, d = x_host.shape
+    if not fused_front_end_ok(d, window):
+        raise ValueError(f"same_l_attention_from_host: needs d_model a multiple of 64 in [64, 512] and window <= 128 "
+                         f"(d_model={d}, window={window})")
+    before = layout["before"] if layout else 0
+    after = layout["after"] if layout else 0
+    rows = before + own + after
+    width, out_w = 5 * num_heads * 64, num_heads * 64
+    if out_host is None:
+        out_host = torch.empty(batch, own, out_w, dtype=torch.bfloat16).pin_memory()
+    if dev_x is None:
+        dev_x = torch.empty(batch, own, d, dtype=torch.bfloat16, device=device)
+    if dev_qkv is None:
+        dev_qkv = torch.empty(batch, rows, width, dtype=torch.bfloat16, device=device)
+    if dev_att is None:
+        dev_att = torch.empty(batch, own, out_w, dtype=torch.bfloat16, device=device)
+    if to_out is not None and dev_out is None:
+        dev_out = torch.empty(batch, own, out_w, dtype=torch.bfloat16, device=device)
+    qn = q_norm if isinstance(q_norm, torch.Tensor) else pack_norm(q_norm, device)
+    kn = k_norm if isinstance(k_norm, torch.Tensor) else pack_norm(k_norm, device)
+    pre = None
+    if pre_norm is not None:
+        pre = pre_norm if isinstance(pre_norm, torch.Tensor) else pack_pre_norm(pre_norm, d, device)
+    freqs = inv_freq.to(device=device, dtype=torch.float32).contiguous()
+    main = torch.cuda.current_stream(device)
+    s_in, s_out = _copy_streams(device)
+    s_in.wait_stream(main)
+    s_out.wait_stream(main)
+    pos_base = (layout["pos0"] if layout else 0) + before  # global position of own row 0
+
+    def project(b: int, r0: int, r1: int) -> None:  # own rows [r0, r1) of batch b, already on the device
+        qkv_project(dev_x[b:b + 1, r0:r1], to_qkv, qn, kn, freqs, num_heads, pre_norm=pre, prepare=True,
+                    pos0=pos_base + r0, out=dev_qkv[b:b + 1, before + r0:before + r1])
+
+    def fetch(b: int, r0: int, r1: int) -> None:
+        with torch.cuda.stream(s_in):
+            dev_x[b, r0:r1].copy_(x_host[b, r0:r1], non_blocking=True)
+
+    chunk = max(128, chunk_rows // 128 * 128)
+    nl = nr = 0  # own rows the left / right neighbour needs (projected first when sharded)
+    if layout and layout["world"] > 1:
+        # the rows the neighbours need first (every batch element), projected, then one halo exchange
+        from hummingbird_b200 import parallel as par
+        w, rk, length, win = layout["world"], comm.rank, layout["length"], layout["window"]
+        nl = par.band_layout(length, w, rk - 1, win)["after"] if rk > 0 else 0
+        nr = par.band_layout(length, w, rk + 1, win)["before"] if rk < w - 1 else 0
+        for b in range(batch):
+            if nl:
+                fetch(b, 0, nl)
+            if nr:
+                fetch(b, own - nr, own)
+        main.wait_stream(s_in)
+        for b in range(batch):
+            if nl:
+                project(b, 0, nl)
+            if nr:
+                project(b, own - nr, own)
+        comm.halo_exchange(dev_qkv, layout)
+    for b in range(batch):
+        done, tail_done = nl, own - nr  # own rows [0, done) and [tail_done, own) are projected
+        for c0 in range(0, own, chunk):
+            c1 = min(own, c0 + chunk)
+            # whole key tiles up to `window` rows past the chunk (buffer coordinates), within the own rows
+            need = min(own, -(-(before + c1 + window) // 128) * 128 - before)
+            hi = min(need, tail_done)
+            if hi > done:
+                fetch(b, done, hi)
+                main.wait_stream(s_in)
+                project(b, done, hi)
+                done = hi
+            band_attention_prepared(dev_qkv[b:b + 1], num_heads, window, q_begin=before + c0, q_count=c1 - c0,
+                                    lam=lam, out=dev_att[b:b + 1, c0:c1])
+            res = dev_att
+            if to_out is not None:
+                torch.matmul(dev_att[b, c0:c1], to_out.t(), out=dev_out[b, c0:c1])
+                res = dev_out
+            s_out.wait_stream(main)
+            with torch.cuda.stream(s_out):
+                out_host[b, c0:c1].copy_(res[b, c0:c1], non_blocking=True)
+    main.wait_stream(s_out)
+    return out_host

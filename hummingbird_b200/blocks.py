@@ -43,13 +43,32 @@ def dit_self_attention(h: torch.Tensor, attn: dict, static: dict, cfg: DiTConfig
     return _linear(out, attn["to_out"]["weight"])
 
 
-def same_l_attention(x: torch.Tensor, block: dict, cfg: SameConfig, lam: torch.Tensor | None = None) -> torch.Tensor:
-    """`block["self_attn"]` holds `to_qkv`, `q_norm`/`k_norm` DyT dicts and `to_out`; `block["rope_inv_freq"]`."""
+def same_l_attention(x: torch.Tensor, block: dict, cfg: SameConfig, lam: torch.Tensor | None = None,
+                     pre_norm: dict | None = None) -> torch.Tensor:
+    """`same_l._attention` (same_l.py:151-161). `block["self_attn"]` holds `to_qkv`, `q_norm`/`k_norm` DyT dicts
+    and `to_out`; `block["rope_inv_freq"]`. x is `_attention`'s input (`_block` has applied its DyT pre-norm)
+    unless `pre_norm` (`block["pre_norm"]`) is given: x is then the block input and the pre-norm runs inside the
+    front end (same_l.py:191).
+
+    With d_model <= 512 and window <= 128 the projection runs as the one-GEMM front end (pre-norm, `to_qkv`,
+    q/k DyT + RoPE) and the band kernel reads its prepared output; otherwise `to_qkv` is a bf16 matmul and the
+    band kernel prepares q/k itself. `to_out` is a bf16 matmul."""
     _require_cuda(cfg.attention)
     attn = block["self_attn"]
-    qkv = _linear(x, attn["to_qkv"]["weight"])
-    out = _band.band_attention(qkv, attn["q_norm"], attn["k_norm"], block["rope_inv_freq"], cfg.num_heads,
-                               cfg.dim_heads, cfg.sub_chunk_size, lam=lam)
+    window = cfg.sub_chunk_size
+    if _band.fused_front_end_ok(x.shape[-1], window):
+        out = _band.same_l_attention_x(x, attn["to_qkv"]["weight"], attn["q_norm"], attn["k_norm"],
+                                       block["rope_inv_freq"], cfg.num_heads, window, pre_norm=pre_norm, lam=lam)
+    else:
+        if pre_norm is not None:  # `_dyt(x, pre_norm).astype(compute)` in fp32
+            f32 = torch.float32
+            alpha = torch.as_tensor(pre_norm["alpha"], dtype=f32, device=x.device)
+            gamma = torch.as_tensor(pre_norm["gamma"], dtype=f32, device=x.device)
+            beta = torch.as_tensor(pre_norm["beta"], dtype=f32, device=x.device)
+            x = (gamma * torch.tanh(alpha * x.to(f32)) + beta).to(x.dtype)
+        qkv = _linear(x, attn["to_qkv"]["weight"])
+        out = _band.band_attention(qkv, attn["q_norm"], attn["k_norm"], block["rope_inv_freq"], cfg.num_heads,
+                                   cfg.dim_heads, window, lam=lam)
     return _linear(out, attn["to_out"]["weight"])
 
 

@@ -102,6 +102,7 @@ def band_inputs(device, *, seed=1, batch=1, length=82_688, d_model=512, heads=8,
 class BandLayerInputs:
     x: torch.Tensor            # (B, L, d) bf16: the block input before its DyT pre-norm
     to_qkv: torch.Tensor       # (5 H 64, d) bf16, the checkpoint's [out, in]
+    to_out: torch.Tensor       # (H 64, H 64) bf16
     pre_norm: dict             # block DyT {"alpha", "gamma" (d,), "beta" (d,)}
     q_norm: dict
     k_norm: dict
@@ -111,11 +112,16 @@ class BandLayerInputs:
     window: int
 
 
-def band_layer_inputs(device, *, seed=11, batch=1, length=82_688, d_model=512, heads=8, half=16, window=128):
-    """The SAME-L attention layer's own inputs (x and the to_qkv weight) for the one-GEMM front end."""
+def band_layer_inputs(device, *, seed=11, batch=1, length=82_688, d_model=512, heads=8, half=16, window=128,
+                      x_seed=None):
+    """The SAME-L attention layer's own inputs (x, the to_qkv / to_out weights) for the one-GEMM front end.
+    `x_seed` (e.g. `(seed, rank)`) draws other rows of the same sequence with the same weights."""
     rng = np.random.default_rng(seed)
     bf = lambda a: torch.from_numpy(np.asarray(a, np.float32)).to(device).to(torch.bfloat16)  # noqa: E731
-    x = bf(rng.standard_normal((batch, length, d_model), dtype=np.float32))
+    x = rng.standard_normal((batch, length, d_model), dtype=np.float32)
+    if x_seed is not None:
+        x = np.random.default_rng(x_seed).standard_normal((batch, length, d_model), dtype=np.float32)
+    x = bf(x)
     w = bf(np.concatenate([rng.standard_normal((heads * 64, d_model), dtype=np.float32) / np.sqrt(d_model)
                            for _ in range(5)]))
     pre = {"alpha": np.float32(0.5), "gamma": (1.0 + 0.02 * rng.standard_normal(d_model)).astype(np.float32),
@@ -127,7 +133,8 @@ def band_layer_inputs(device, *, seed=11, batch=1, length=82_688, d_model=512, h
 
     qn, kn = norm(), norm()
     lam = rng.uniform(0.2, 0.8, heads // 2).astype(np.float32)
-    return BandLayerInputs(x, w, pre, qn, kn, inv_freq(half), lam, heads, window)
+    to_out = bf(rng.standard_normal((heads * 64, heads * 64), dtype=np.float32) / np.sqrt(heads * 64))
+    return BandLayerInputs(x, w, to_out, pre, qn, kn, inv_freq(half), lam, heads, window)
 
 
 @dataclass

@@ -118,6 +118,80 @@ def time_band_sample(qkv: np.ndarray, q_norm: dict, k_norm: dict, freqs: np.ndar
             "cores": _WORKERS}
 
 
+def _front_task(args):
+    from oracle.band import front_end
+    xname, xshape, qname, qshape, w_qkv, pre, r0, r1 = args
+    x = _attach_many(xname, xshape)
+    qkv = _attach_many(qname, qshape)
+    qkv[:, r0:r1] = front_end(x[:, r0:r1], w_qkv, pre)
+    return r1 - r0
+
+
+def _layer_task(args):
+    from oracle.band import band_diff_attention
+    qname, qshape, qn, kn, freqs, heads, window, lam, w_out, lo, hi, q0, q1 = args
+    qkv = _attach_many(qname, qshape)[:, lo:hi]
+    out = band_diff_attention(qkv, qn, kn, freqs, heads, window, lam=lam, offset=lo, dtype=np.float32)
+    y = out[:, q0 - lo:q1 - lo] @ w_out.T
+    return float(y.sum())
+
+
+_SHM_MANY: dict = {}
+
+
+def _attach_many(name: str, shape: tuple) -> np.ndarray:
+    from multiprocessing import shared_memory
+    if name not in _SHM_MANY:
+        if len(_SHM_MANY) > 8:
+            _SHM_MANY.clear()
+        shm = shared_memory.SharedMemory(name=name)
+        _SHM_MANY[name] = (shm, np.ndarray(shape, np.float32, buffer=shm.buf))
+    return _SHM_MANY[name][1]
+
+
+def time_layer_sample(x: np.ndarray, w_qkv: np.ndarray, w_out: np.ndarray, pre_norm: dict | None, q_norm: dict,
+                      k_norm: dict, freqs: np.ndarray, heads: int, window: int, lam: np.ndarray, q_rows: int,
+                      workers: int | None = None, chunk: int = 256, min_seconds: float = 0.0) -> dict:
+    """Time the SAME-L attention layer's oracle (`oracle.band.front_end`: block DyT pre-norm + `to_qkv`; the
+    band attention; `to_out`) on queries [0, q_rows) of x (float32 `(1, L, d)` holding bf16 values) over a spawn
+    pool: phase 1 projects the rows the sample needs once, in `chunk`-row tasks, into a shared array; phase 2
+    runs the band attention and `to_out` per `chunk` of queries. Repeats the whole sample until `min_seconds`
+    have passed (at least once). FLOPs counted: the attention's only (as for `time_band_sample`)."""
+    from multiprocessing import shared_memory
+    length = x.shape[1]
+    rows = min(length, q_rows + window)
+    n = w_qkv.shape[0]
+    p = pool(workers)
+    xs = shared_memory.SharedMemory(create=True, size=x[:, :rows].nbytes)
+    qs = shared_memory.SharedMemory(create=True, size=rows * n * 4)
+    try:
+        xshape, qshape = (1, rows, x.shape[2]), (1, rows, n)
+        np.ndarray(xshape, np.float32, buffer=xs.buf)[...] = x[:, :rows]
+        front = [(xs.name, xshape, qs.name, qshape, w_qkv, pre_norm, r0, min(rows, r0 + chunk))
+                 for r0 in range(0, rows, chunk)]
+        layer = []
+        for q0 in range(0, q_rows, chunk):
+            q1 = min(q_rows, q0 + chunk)
+            lo, hi = max(0, q0 - window), min(rows, q1 + window)
+            layer.append((qs.name, qshape, q_norm, k_norm, freqs, heads, window, lam, w_out, lo, hi, q0, q1))
+        p.map(_front_task, front[: min(len(front), _WORKERS)])  # warm the workers
+        t0 = time.perf_counter()
+        passes = 0
+        while True:
+            p.map(_front_task, front)
+            p.map(_layer_task, layer)
+            passes += 1
+            if time.perf_counter() - t0 >= min_seconds:
+                break
+        seconds = time.perf_counter() - t0
+    finally:
+        for shm in (xs, qs):
+            shm.close()
+            shm.unlink()
+    return {"seconds": seconds, "flops": passes * band_flops(length, heads, window, 0, q_rows), "passes": passes,
+            "cores": _WORKERS}
+
+
 def _dense_task(args):
     from oracle.dense import dense_branches
     qkv, q_w, k_w, freqs, valid, heads, eps = args

@@ -129,3 +129,27 @@ def test_front_end_config2_full_length(cuda_lib):
         ref = oband.band_diff_attention(qkv[:, lo:hi], w.q_norm, w.k_norm, w.inv_freq, w.heads, w.window, lam=w.lam,
                                         offset=lo)
         check_attn(out[:, s:s + 384], ref[:, s - lo:s - lo + 384])
+
+
+def test_layer_from_host_equals_device_call(cuda_lib):
+    """`same_l_attention_from_host` (pinned host x streamed in 256-row chunks, projected per chunk at its
+    positions, band kernel per chunk of queries, rows copied back) equals the device call `same_l_attention_x`
+    bit for bit, for two batch elements; with `to_out` (a bf16 matmul per chunk) it matches the device call
+    followed by one `to_out` matmul within a bf16 rounding (the library may pick another GEMM per row count)."""
+    from hummingbird_b200.band_attention import same_l_attention_from_host, same_l_attention_x
+    w = _inputs(batch=2, length=1000, d_model=256, heads=4)
+    freqs, lam = f32_cuda(w.inv_freq), f32_cuda(w.lam)
+    g = torch.Generator(device="cuda").manual_seed(5)
+    to_out = (torch.randn(256, 256, generator=g, device="cuda") / 16).to(torch.bfloat16)
+    dev = same_l_attention_x(w.x, w.to_qkv, w.q_norm, w.k_norm, freqs, w.heads, w.window, pre_norm=w.pre_norm,
+                             lam=lam)
+    x_host = w.x.cpu().pin_memory()
+    kw = dict(pre_norm=w.pre_norm, lam=lam, chunk_rows=256)
+    out = same_l_attention_from_host(x_host, w.to_qkv, w.q_norm, w.k_norm, freqs, w.heads, w.window, **kw)
+    torch.cuda.synchronize()
+    assert torch.equal(out, dev.cpu())
+    out = same_l_attention_from_host(x_host, w.to_qkv, w.q_norm, w.k_norm, freqs, w.heads, w.window, to_out=to_out,
+                                     **kw)
+    torch.cuda.synchronize()
+    ref = torch.stack([dev[b] @ to_out.t() for b in range(2)]).float().cpu()
+    assert torch.allclose(out.float(), ref, rtol=2 ** -7, atol=1e-6)

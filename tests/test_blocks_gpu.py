@@ -42,10 +42,34 @@ def test_same_l_attention_call_site(cuda_lib):
                            "to_out": {"weight": torch.eye(256, device="cuda", dtype=torch.bfloat16)},
                            "q_norm": norm, "k_norm": norm},
              "rope_inv_freq": torch.from_numpy(freqs).cuda()}
-    out = blocks.same_l_attention(x, block, cfg)
+    out = blocks.same_l_attention(x, block, cfg)  # d_model 256: the one-GEMM front end
     qkv = to_np(x @ block["self_attn"]["to_qkv"]["weight"].T)
     ref = oband.band_diff_attention(qkv, norm, norm, freqs, 4, cfg.sub_chunk_size)
     check_attn(to_np(out), ref)
+    # with the block's DyT pre-norm inside the front end, against `oracle.band.front_end` (same_l.py:191)
+    pre = {"alpha": np.float32(0.5), "gamma": np.full(256, 1.1, np.float32), "beta": np.full(256, 0.01, np.float32)}
+    out = blocks.same_l_attention(x, block, cfg, pre_norm=pre)
+    qkv = oband.front_end(to_np(x), to_np(block["self_attn"]["to_qkv"]["weight"]), pre)
+    check_attn(to_np(out), oband.band_diff_attention(qkv, norm, norm, freqs, 4, cfg.sub_chunk_size))
+
+
+def test_same_l_attention_call_site_wide_model(cuda_lib):
+    """d_model 768 (the reference's default SAME-L width, 12 heads): past the front end's 512, so `to_qkv` is a
+    bf16 matmul and the band kernel prepares q/k itself."""
+    from hummingbird_b200 import blocks
+    from hummingbird_b200.config import SameConfig
+    cfg = SameConfig(channels=128, c_mults=(6,), stride=16)
+    g = torch.Generator(device="cuda").manual_seed(4)
+    x = torch.randn(1, 17 * 12, 768, generator=g, device="cuda").to(torch.bfloat16)
+    norm = {"alpha": np.float32(0.5), "gamma": np.ones(64, np.float32), "beta": np.zeros(64, np.float32)}
+    freqs = odense.inv_freq(cfg.rope_half)
+    block = {"self_attn": {"to_qkv": {"weight": (torch.randn(3840, 768, generator=g, device="cuda") / 28).to(torch.bfloat16)},
+                           "to_out": {"weight": torch.eye(768, device="cuda", dtype=torch.bfloat16)},
+                           "q_norm": norm, "k_norm": norm},
+             "rope_inv_freq": torch.from_numpy(freqs).cuda()}
+    out = blocks.same_l_attention(x, block, cfg)
+    qkv = to_np(x @ block["self_attn"]["to_qkv"]["weight"].T)
+    check_attn(to_np(out), oband.band_diff_attention(qkv, norm, norm, freqs, 12, cfg.sub_chunk_size))
 
 
 def test_w8a8_glu_mlp_close_to_bf16(cuda_lib):
