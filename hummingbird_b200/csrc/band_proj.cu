@@ -22,7 +22,8 @@
 // to one 256-column fp32 accumulator, so only W streams through shared memory: CTA r loads W rows
 // [128 r, 128 r + 128) of each 256 x 64 box into a 9-stage ring (144 KiB in flight per SM covers the L2 latency),
 // and each stage is four MMAs (512 cycles), which hide the stage commits. The last column tile may reach past N:
-// W rows there load as zeros and their head blocks are not stored. Units go to clusters round-robin.
+// W rows there load as zeros and their head blocks are not stored. Units go to clusters round-robin, the column
+// groups of one 256-row tile next to each other (its x tile is read from DRAM once, then from L2).
 // x reaches TMEM through a two-slot shared-memory staging ring: the DyT warps read a landed 128 x 64 chunk (their
 // rows), free the slot, apply the block DyT in registers, wait until the unit before has finished its MMAs on
 // that chunk, and store it to TMEM with tcgen05.st; the next unit's DyT thus runs while the current unit's last
@@ -92,7 +93,7 @@ struct ProjParams {
   const float* q_norm;    // [129]: alpha, gamma[64], beta[64]
   const float* k_norm;
   const float* inv_freq;  // [half]
-  int num_m, tiles_per_group, units;  // num_m: 256-row tiles
+  int num_m, groups, tiles_per_group, units;  // num_m: 256-row tiles; unit u: tile u / groups, group u % groups
 };
 
 template <uint32_t N>
@@ -203,7 +204,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int w_issued = 0;
       bool ok = true;
       for (int u = cluster; ok && u < p.units; u += clusters) {
-        const int g = u / p.num_m;
+        const int g = u % p.groups;
         for (int t = 0; ok && t < tpg; ++t) {
           const int n0 = (g * tpg + t) * kBN + static_cast<int>(rank) * kWRows;
           for (int c = 0; c < nkc; ++c) {
@@ -229,7 +230,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int q = 0;
       bool ok = true;
       for (int u = cluster; ok && u < p.units; u += clusters) {
-        const int m0 = (u % p.num_m) * 2 * kBM + static_cast<int>(rank) * kBM;
+        const int m0 = (u / p.groups) * 2 * kBM + static_cast<int>(rank) * kBM;
         for (int c = 0; c < nkc; ++c, ++q) {
           const int slot = q % kXSlots;
           if (q >= kXSlots && !mbar_wait_sleep(&x_free[slot], ((q / kXSlots) & 1) ^ 1, 100)) {
@@ -357,7 +358,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     int tl = 0;
     bool ok = true;
     for (int u = cluster; ok && u < p.units; u += clusters) {
-      const int m0 = (u % p.num_m) * 2 * kBM + static_cast<int>(rank) * kBM, g = u / p.num_m;
+      const int m0 = (u / p.groups) * 2 * kBM + static_cast<int>(rank) * kBM, g = u % p.groups;
       const int m = m0 + r;
       const float pos = static_cast<float>(p.pos0 + (m % p.rows));
       for (int t = 0; t < tpg; ++t, ++tl) {
@@ -546,6 +547,7 @@ extern "C" int hb_band_qkv_project(const void* x, int64_t ldx, const float* pre_
   const int ntn = (N + kBN - 1) / kBN;
   const int pairs = sms / 2;
   const int groups = choose_groups(p.num_m, ntn, pairs, 0.5);
+  p.groups = groups;
   p.tiles_per_group = ntn / groups;
   p.units = p.num_m * groups;
   const int clusters = p.units < pairs ? p.units : pairs;
