@@ -1,6 +1,7 @@
 """GPU parity for the W8A8 path through the C ABI: quantisation, int32 accumulators and the bf16 epilogue are
 all bit-exact against the CPU oracle (oracle/w8a8.py). Shapes with K >= 8192 and M >= 1024 run the CTA-pair
-kernel (ragged M, N and K included); the others the one-CTA kernel."""
+kernel (ragged M, N and K included); the others the one-CTA kernel. Each shape also runs without the int32
+accumulator copy and without bias."""
 import numpy as np
 import pytest
 import torch
@@ -34,7 +35,8 @@ def test_w8a8_golden_bit_exact(cuda_lib):
 
 
 @pytest.mark.parametrize("m,k,n", [(2584, 1024, 4096), (2584, 4096, 1024), (1100, 8192, 1024), (1030, 8208, 352),
-                                   (1300, 512, 1024), (513, 272, 96), (200, 272, 96), (1, 16, 32)])
+                                   (1300, 512, 1024), (513, 272, 96), (200, 272, 96), (1, 16, 32), (300, 384, 320),
+                                   (1, 128, 64), (5296, 1024, 5120)])
 def test_w8a8_gemm_bit_exact(m, k, n, cuda_lib):
     from hummingbird_b200.w8a8 import quantize_rows, w8a8_gemm
     g = torch.Generator(device="cuda").manual_seed(m * 7 + k * 3 + n)
@@ -54,6 +56,12 @@ def test_w8a8_gemm_bit_exact(m, k, n, cuda_lib):
     assert np.array_equal(acc.cpu().numpy(), acc_ref)
     y_ref = ow.epilogue(acc_ref, sx_ref, sw_ref, bits_np(bias))
     assert np.array_equal(bits_np(y), y_ref)
+    # without the accumulator copy, and without bias
+    y2 = w8a8_gemm(qx, sx, qw, sw, bias)
+    y3 = w8a8_gemm(qx, sx, qw, sw, None)
+    torch.cuda.synchronize()
+    assert np.array_equal(bits_np(y2), y_ref)
+    assert np.array_equal(bits_np(y3), ow.epilogue(acc_ref, sx_ref, sw_ref, None))
 
 
 def test_w8a8_linear_pair_config3(cuda_lib):
