@@ -1029,7 +1029,7 @@ def main():
             "d2h_bytes_per_step": e2e_l["d2h"],
             "how": "same_l_attention_from_host: the SAME-L attention layer (same_l._attention of _block: block DyT "
                    "pre-norm, to_qkv, band attention, to_out) with its input x in pinned host memory, streamed in "
-                   "8,192-row chunks through the one-GEMM front end and the band kernel; attention FLOPs counted",
+                   "16,384-row chunks through the one-GEMM front end and the band kernel; attention FLOPs counted",
             "device_ms_per_step": tl["ms_per_step"],
             "device_stages_ms": {"front_end": tl["proj_ms"], "band": tl["attn_ms"], "to_out": tl["to_out_ms"]},
             "front_end_roofline": {"bound": "tensor", "kernel": "band_proj_kernel",

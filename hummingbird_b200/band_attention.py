@@ -256,7 +256,7 @@ def same_l_attention_from_host(x_host: torch.Tensor, to_qkv: torch.Tensor, q_nor
                                lam: torch.Tensor | None = None, out_host: torch.Tensor | None = None,
                                dev_x: torch.Tensor | None = None, dev_qkv: torch.Tensor | None = None,
                                dev_att: torch.Tensor | None = None, dev_out: torch.Tensor | None = None,
-                               layout: dict | None = None, comm=None, chunk_rows: int = 8192) -> torch.Tensor:
+                               layout: dict | None = None, comm=None, chunk_rows: int = 16384) -> torch.Tensor:
     """`same_l._attention` (same_l.py:151-161) of a layer input held in pinned HOST memory: x `(B, R, d)` bf16
     streams to the device in chunks; each chunk's rows go through the one-GEMM front end (`qkv_project`,
     prepared, at their sequence positions); a chunk's queries run through the band kernel once the rows up to
