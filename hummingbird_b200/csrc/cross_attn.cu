@@ -99,8 +99,22 @@ __device__ __forceinline__ Unit decode(const CrossParams& p, int u) {
 
 __device__ __forceinline__ bool same_run(const Unit& a, const Unit& b) { return a.b == b.b && a.h == b.h; }
 
-__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
-  const bool ok = mbar_wait(bar, parity) && !*abort_flag;
+// Polls of the roles with slack (the TMA producer, the RMSNorm / epilogue warps) and of the softmax sleep between
+// tries, so waiting warps leave issue slots to the working ones; the MMA thread polls without sleeping.
+#ifndef HB_CROSS_SLACK_SLEEP_NS
+#define HB_CROSS_SLACK_SLEEP_NS 200
+#endif
+#ifndef HB_CROSS_SOFT_SLEEP_NS
+#define HB_CROSS_SOFT_SLEEP_NS 100
+#endif
+constexpr unsigned kSlackSleepNs = HB_CROSS_SLACK_SLEEP_NS, kSoftSleepNs = HB_CROSS_SOFT_SLEEP_NS;
+
+__device__ __forceinline__ bool sleep_wait(uint64_t* bar, uint32_t parity, unsigned sleep_ns) {
+  return sleep_ns ? mbar_wait_sleep(bar, parity, sleep_ns) : mbar_wait(bar, parity);
+}
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                          unsigned sleep_ns = kSlackSleepNs) {
+  const bool ok = sleep_wait(bar, parity, sleep_ns) && !*abort_flag;
   return __all_sync(0xffffffffu, ok);
 }
 
@@ -260,7 +274,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (bh != prev_bh) {
           prev_bh = bh;
           ++run;
-          if (run >= 1 && !mbar_wait(kv_empty, (run - 1) & 1)) {
+          if (run >= 1 && !sleep_wait(kv_empty, (run - 1) & 1, kSlackSleepNs)) {
             *abort_flag = 1;
             break;
           }
@@ -275,7 +289,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           XT(0, 200 + run);
         }
         const int qb = j & 1;
-        if (j >= 2 && !mbar_wait(&q_empty[qb], ((j >> 1) & 1) ^ 1)) {
+        if (j >= 2 && !sleep_wait(&q_empty[qb], ((j >> 1) & 1) ^ 1, kSlackSleepNs)) {
           *abort_flag = 1;
           break;
         }
@@ -402,7 +416,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t tO = tmem + lane_base + 256u + 128u * (j & 1) + (br ? 64u : 0u);
       float m = -INFINITY, l = 0.f;
       for (int kt = 0; kt < p.nkt; ++kt, ++t) {
-        if (!(ok = warp_wait(&s_full[br], t & 1, abort_flag))) break;
+        if (!(ok = warp_wait(&s_full[br], t & 1, abort_flag, kSoftSleepNs))) break;
         if (lane == 0 && quad == 0) XT(2 + br, 100 + t);
         tc_fence_after();
         const int k0 = kt * kTileRows;
