@@ -1,8 +1,8 @@
 // Dense differential self-attention (the DiT's `dense_attention`), C-ABI front end + its prologue.
 //
-// Prologue (`dense_prep_kernel`, HBM-bound): reads the `to_qkv` output once with 128-bit loads (several per
-// thread in flight) and writes
-// per-(batch, head, section) 128-row tiles in the SW128 UMMA image:
+// Prologue (`dense_prep_kernel`, HBM-bound): reads the `to_qkv` output once with 128-bit loads (a warp takes
+// one row for four heads, all five sections' loads in flight together, the row's lane-table chunks loaded once)
+// and writes per-(batch, head, section) 128-row tiles in the SW128 UMMA image:
 //   q, k, q_diff, k_diff: RMSNorm in fp32 over the head's 64 dims -> bf16 -> RoPE in fp32 with the
 //                         caller's cos / signed-sin lane tables -> bf16   (dense_attention.py:61-69)
 //   v:                    bf16(v * mask)                                   (dense_attention.py:77)
@@ -21,7 +21,7 @@ namespace hb {
 namespace {
 
 constexpr int kPrepThreads = 256;
-constexpr int kUnitsPerGroup = 4;  // units (one row x one section x one head) per 8-thread group, loads issued together
+constexpr int kHeadsPerWarp = 4;  // a warp: one row, four heads (an 8-lane group per head, 16 bytes per lane)
 
 // n / d for 0 <= n < 2^31 by a multiply-high and a shift (the round-up reciprocal method: multiplier
 // ceil(2^p / d) with p = 31 + ceil(log2 d)); replaces the integer divisions of the unit decode.
@@ -58,25 +58,10 @@ struct DensePrepParams {
   int half;
   uint8_t* ws;
   int ntiles;
-  int units;  // B * ntiles * 128 * 5 * heads (< 2^31, checked on the host)
-  FastDiv by_heads, by_sections, by_rows;
+  int hgroups;  // ceil(heads / kHeadsPerWarp)
+  int tasks;    // B * ntiles * 128 * hgroups (< 2^31, checked on the host)
+  FastDiv by_hgroups, by_rows;
 };
-
-struct UnitPos {
-  int hl, s, row, b;
-};
-
-__device__ __forceinline__ UnitPos decode_unit(const DensePrepParams& p, uint32_t u) {
-  UnitPos x;
-  const uint32_t rs = p.by_heads(u);
-  x.hl = static_cast<int>(u - rs * static_cast<uint32_t>(p.heads));
-  const uint32_t br = p.by_sections(rs);
-  x.s = static_cast<int>(rs - br * kSections);
-  const uint32_t bb = p.by_rows(br);
-  x.row = static_cast<int>(br - bb * static_cast<uint32_t>(p.ntiles * kTileRows));
-  x.b = static_cast<int>(bb);
-  return x;
-}
 
 // 8 consecutive fp32 values; 16-byte vector loads when kVec (the caller checked the alignment)
 template <bool kVec>
@@ -92,41 +77,51 @@ __device__ __forceinline__ void load8f(const float* src, float (&v)[8]) {
   }
 }
 
-// Unit u = ((b * rows_pad + row) * 5 + section) * heads + head: consecutive 8-thread groups take consecutive
-// units (consecutive 128-byte pieces of a qkv row), and each group takes kUnitsPerGroup units spaced a grid
-// apart, loading all of them before computing.
+// Task t = (b * rows_pad + row) * hgroups + hg, one warp each: lane = 8 * hsub + c takes the 16-byte chunk c of
+// head 4 hg + hsub in all five sections of the row. The row's cos / sin chunks and the weight chunks are loaded
+// once per task; the five data loads are issued before any computing. Padding rows (row >= L) are written as
+// zeros, as the attention kernel expects.
 template <bool kVec>
-__global__ void __launch_bounds__(kPrepThreads) dense_prep_kernel(const DensePrepParams p) {
+__global__ void __launch_bounds__(kPrepThreads, 3) dense_prep_kernel(const DensePrepParams p) {
   const int lane = threadIdx.x & 31;
-  const int c = threadIdx.x & 7;
+  const int c = lane & 7, hsub = lane >> 3;
   const unsigned gmask = 0xFFu << (lane & 24);
   const int hc8 = p.half >> 3;
-  const int group = blockIdx.x * (kPrepThreads / 8) + (threadIdx.x >> 3);
-  const int stride = gridDim.x * (kPrepThreads / 8);
-  uint4 raw[kUnitsPerGroup];
+  const int task = blockIdx.x * (kPrepThreads / 32) + (threadIdx.x >> 5);
+  if (task >= p.tasks) return;  // warp-uniform
+  const uint32_t br = p.by_hgroups(static_cast<uint32_t>(task));
+  const int hl = static_cast<int>(task - br * static_cast<uint32_t>(p.hgroups)) * kHeadsPerWarp + hsub;
+  if (hl >= p.heads) return;  // the whole 8-lane group (its shuffles involve only its own lanes)
+  const uint32_t bb = p.by_rows(br);
+  const int row = static_cast<int>(br - bb * static_cast<uint32_t>(p.ntiles * kTileRows));
+  const int b = static_cast<int>(bb);
+  const bool valid = row < p.L;
+  uint4 raw[kSections];
+  if (valid) {
+    const uint16_t* src = p.qkv + ((size_t)b * p.L + row) * p.qkv_row_stride + (size_t)(p.head0 + hl) * kHeadDim + c * 8;
 #pragma unroll
-  for (int k = 0; k < kUnitsPerGroup; ++k) {
-    const int u = group + k * stride;
-    raw[k] = make_uint4(0, 0, 0, 0);
-    if (u < p.units) {
-      const UnitPos x = decode_unit(p, static_cast<uint32_t>(u));
-      if (x.row < p.L)
-        raw[k] = ld_nc_v4(p.qkv + ((size_t)x.b * p.L + x.row) * p.qkv_row_stride + (size_t)x.s * p.H_total * kHeadDim +
-                          (size_t)(p.head0 + x.hl) * kHeadDim + c * 8);
-    }
+    for (int s = 0; s < kSections; ++s) raw[s] = ld_nc_v4(src + (size_t)s * p.H_total * kHeadDim);
+  } else {
+#pragma unroll
+    for (int s = 0; s < kSections; ++s) raw[s] = make_uint4(0, 0, 0, 0);
   }
+  float cr[8], sr[8], qwv[8], kwv[8];
+  if (valid) {
+    load8f<kVec>(p.cos + (size_t)row * p.table_stride + c * 8, cr);
+    load8f<kVec>(p.sin + (size_t)row * p.table_stride + c * 8, sr);
+  }
+  load8f<kVec>(p.q_w + c * 8, qwv);
+  load8f<kVec>(p.k_w + c * 8, kwv);
+  const float m = valid ? __uint_as_float((uint32_t)p.vmask[b * p.mask_bstride + row * p.mask_lstride] << 16) : 0.f;
+  const int src_lane = (lane & 24) | rope_partner_chunk(c, hc8);
+  uint8_t* dst = p.ws + prep_tile_offset(b, hl, 0, row / kTileRows, p.heads, p.ntiles) + sw128_offset(row % kTileRows, c);
+  const size_t sec_bytes = (size_t)p.ntiles * kTileBytes;
 #pragma unroll
-  for (int k = 0; k < kUnitsPerGroup; ++k) {
-    const int u = group + k * stride;
-    if (u >= p.units) break;  // uniform within the 8-thread group (same u)
-    const UnitPos x = decode_unit(p, static_cast<uint32_t>(u));
-    const bool valid = x.row < p.L;
+  for (int s = 0; s < kSections; ++s) {
     float xv[8];
-    unpack8(raw[k], xv);
+    unpack8(raw[s], xv);
     uint4 outv;
-    if (x.s == 2) {
-      const float m = valid ? __uint_as_float((uint32_t)p.vmask[x.b * p.mask_bstride + x.row * p.mask_lstride] << 16)
-                            : 0.f;
+    if (s == 2) {  // v * mask
 #pragma unroll
       for (int i = 0; i < 8; ++i) xv[i] *= m;
       outv = pack8(xv);
@@ -138,27 +133,23 @@ __global__ void __launch_bounds__(kPrepThreads) dense_prep_kernel(const DensePre
       ss += __shfl_xor_sync(gmask, ss, 2);
       ss += __shfl_xor_sync(gmask, ss, 4);
       const float inv = rsqrtf(ss * (1.f / kHeadDim) + p.eps);
-      float wv[8], y[8];
-      load8f<kVec>(((x.s == 0 || x.s == 3) ? p.q_w : p.k_w) + c * 8, wv);
+      const float* wv = (s == 0 || s == 3) ? qwv : kwv;
+      float y[8];
 #pragma unroll
       for (int i = 0; i < 8; i += 2) {  // (x * inv) * w, each product rounded (packed pairs)
         fmul2(y[i], y[i + 1], xv[i], xv[i + 1], inv, inv);
         fmul2(y[i], y[i + 1], y[i], y[i + 1], wv[i], wv[i + 1]);
       }
       const uint4 yb = pack8(y);  // RMSNorm output rounded to bf16 (dense_attention.py:66)
-      const int src = (lane & 24) | rope_partner_chunk(c, hc8);
       uint4 pb;
-      pb.x = __shfl_sync(gmask, yb.x, src);
-      pb.y = __shfl_sync(gmask, yb.y, src);
-      pb.z = __shfl_sync(gmask, yb.z, src);
-      pb.w = __shfl_sync(gmask, yb.w, src);
+      pb.x = __shfl_sync(gmask, yb.x, src_lane);
+      pb.y = __shfl_sync(gmask, yb.y, src_lane);
+      pb.z = __shfl_sync(gmask, yb.z, src_lane);
+      pb.w = __shfl_sync(gmask, yb.w, src_lane);
       float yv[8], pv[8];
       unpack8(yb, yv);
       unpack8(pb, pv);
       if (valid) {
-        float cr[8], sr[8];
-        load8f<kVec>(p.cos + (size_t)x.row * p.table_stride + c * 8, cr);
-        load8f<kVec>(p.sin + (size_t)x.row * p.table_stride + c * 8, sr);
 #pragma unroll
         for (int i = 0; i < 8; i += 2) {  // y cos + partner * signed sin
           float t0, t1;
@@ -171,9 +162,7 @@ __global__ void __launch_bounds__(kPrepThreads) dense_prep_kernel(const DensePre
       }
       outv = pack8(y);
     }
-    uint8_t* dst = p.ws + prep_tile_offset(x.b, x.hl, x.s, x.row / kTileRows, p.heads, p.ntiles) +
-                   sw128_offset(x.row % kTileRows, c);
-    *reinterpret_cast<uint4*>(dst) = outv;
+    *reinterpret_cast<uint4*>(dst + s * sec_bytes) = outv;
   }
 }
 
@@ -225,17 +214,16 @@ extern "C" int hb_dense_diff_attn(const void* qkv, int64_t qkv_row_stride, const
   if (st != HB_OK) return st;
 
   const int ntiles = (length + kTileRows - 1) / kTileRows;
-  const int64_t units = (int64_t)batch * ntiles * kTileRows * kSections * heads;
-  if (units >= (int64_t(1) << 31)) return HB_ERR_SHAPE;
+  const int hgroups = (heads + kHeadsPerWarp - 1) / kHeadsPerWarp;
+  const int64_t tasks = (int64_t)batch * ntiles * kTileRows * hgroups;
+  if (tasks >= (int64_t(1) << 31)) return HB_ERR_SHAPE;
   DensePrepParams pp{static_cast<const uint16_t*>(qkv), qkv_row_stride, batch, length, num_heads, 2 * pair_begin,
                      heads, q_weight, k_weight, cos, sin, table_stride, static_cast<const uint16_t*>(vmask),
-                     mask_batch_stride, mask_row_stride, eps, half, static_cast<uint8_t*>(workspace), ntiles, (int)units,
-                     {}, {}, {}};
-  pp.by_heads.init(static_cast<uint32_t>(heads));
-  pp.by_sections.init(kSections);
+                     mask_batch_stride, mask_row_stride, eps, half, static_cast<uint8_t*>(workspace), ntiles, hgroups,
+                     (int)tasks, {}, {}};
+  pp.by_hgroups.init(static_cast<uint32_t>(hgroups));
   pp.by_rows.init(static_cast<uint32_t>(ntiles * kTileRows));
-  const int64_t groups = (units + kUnitsPerGroup - 1) / kUnitsPerGroup;
-  const int pblocks = (int)((groups + kPrepThreads / 8 - 1) / (kPrepThreads / 8));
+  const int pblocks = (int)((tasks + kPrepThreads / 32 - 1) / (kPrepThreads / 32));
   // 16-byte loads of the weights and lane tables when their rows are 16-byte aligned
   const bool vec = aligned16(q_weight) && aligned16(k_weight) && aligned16(cos) && aligned16(sin) && table_stride % 4 == 0;
   if (vec)
