@@ -80,6 +80,24 @@ def test_band_config2_full_length(cuda_lib):
         check_attn(out[:, s:s + 384], ref[:, s - lo:s - lo + 384])
 
 
+def test_band_config5_length(cuda_lib):
+    """Config 5's decoder length (L=261,888, the 380 s song; 8 heads, window 128) against the oracle on sampled
+    query blocks, the last block included. RoPE angles reach fp32(261,887) * inv_freq here, so this checks the
+    angle reduction far beyond config 2's positions. Only the sampled rows are copied to the host."""
+    from hummingbird_b200.band_attention import band_attention
+    from hummingbird_b200.workloads import band_inputs
+    w = band_inputs("cuda", length=261_888)
+    out = band_attention(w.qkv, w.q_norm, w.k_norm, f32_cuda(w.inv_freq), w.heads, 64, w.window, lam=f32_cuda(w.lam))
+    length = w.qkv.shape[1]
+    rng = np.random.default_rng(5)
+    starts = sorted({0, length // 2, length - 384, *rng.integers(200_000, length - 384, 3).tolist()})
+    for s in starts:
+        lo, hi = max(0, s - w.window), min(length, s + 384 + w.window)
+        ref = oband.band_diff_attention(to_np(w.qkv[:, lo:hi]), w.q_norm, w.k_norm, w.inv_freq, w.heads, w.window,
+                                        lam=w.lam, offset=lo)
+        check_attn(to_np(out[:, s:s + 384]), ref[:, s - lo:s - lo + 384])
+
+
 def test_band_from_host_streamed_equals_device_call(cuda_lib):
     """The host-streamed API (chunks of rows copied in, computed, copied out on overlapping streams) gives
     the same bits as one device call, for B=2 and a chunk size that does not divide the length."""
