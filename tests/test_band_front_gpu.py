@@ -131,6 +131,26 @@ def test_front_end_config2_full_length(cuda_lib):
         check_attn(out[:, s:s + 384], ref[:, s - lo:s - lo + 384])
 
 
+def test_front_end_config5_length(cuda_lib):
+    """Config 5's decoder length (x (1, 261,888, 512), 8 heads, window 128): the front end's RoPE in the GEMM
+    epilogue must give the band kernel's own preparation bit for bit at positions up to 261,887 too, so the
+    prepared path equals the raw-projection path over the whole output; the last query block matches the oracle
+    on this projection."""
+    from hummingbird_b200.band_attention import band_attention, qkv_project, same_l_attention_x
+    w = _inputs(length=261_888)
+    freqs, lam = f32_cuda(w.inv_freq), f32_cuda(w.lam)
+    out = same_l_attention_x(w.x, w.to_qkv, w.q_norm, w.k_norm, freqs, w.heads, w.window, pre_norm=w.pre_norm,
+                             lam=lam)
+    raw = qkv_project(w.x, w.to_qkv, None, None, None, w.heads, pre_norm=w.pre_norm, prepare=False)
+    assert torch.equal(out, band_attention(raw, w.q_norm, w.k_norm, freqs, w.heads, 64, w.window, lam=lam))
+    length = raw.shape[1]
+    s = length - 384
+    lo = s - w.window
+    ref = oband.band_diff_attention(to_np(raw[:, lo:]), w.q_norm, w.k_norm, w.inv_freq, w.heads, w.window,
+                                    lam=w.lam, offset=lo)
+    check_attn(to_np(out[:, s:]), ref[:, s - lo:])
+
+
 def test_layer_from_host_equals_device_call(cuda_lib):
     """`same_l_attention_from_host` (pinned host x streamed in 256-row chunks, projected per chunk at its
     positions, band kernel per chunk of queries, rows copied back) equals the device call `same_l_attention_x`
