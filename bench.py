@@ -887,6 +887,11 @@ def cpu_band_baseline(qkv_dev, w, q_rows: int, min_seconds: float = 10.0) -> dic
                       f"oracle, {r['cores']}-process spawn pool, {r['seconds']:.1f} s"}
 
 
+# The workload both arms time (the reference arm on the host cores in fp32, this library in bf16 on the GPU).
+WORKLOAD = ("SAME-L band differential attention, config 2 per GPU: B=1, L=82,688 rows/GPU, d_model 512 (8 heads x "
+            "64), window +-128, DyT + RoPE(half 16), bf16")
+
+
 def run_reference(args, result_out):
     """`--impl reference`: the reference's path (its fp32 restatement; JAX is absent) on the host cores."""
     rank, world, _ = dist_env()
@@ -912,8 +917,7 @@ def run_reference(args, result_out):
     line = {"metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": secs / args.steps * 1e3, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
-            "config": {"workload": "band diff-attn, config 2: all 82,688 query rows, 8 heads, window 128 "
-                                   "(bf16 inputs, fp32 compute)"},
+            "config": {"workload": WORKLOAD},
             "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": cores, "kind": "port",
                              "sample": f"{q_rows} queries per step; JAX absent, fp32 numpy restatement of the "
                                        "reference XLA path (oracle/band.py)"},
@@ -1012,8 +1016,7 @@ def main():
         "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": t["ms_per_step"], "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": "SAME-L band differential attention, config 2 per GPU: B=1, L=82,688 rows/GPU, "
-                               "d_model 512 (8 heads x 64), window +-128, DyT + RoPE(half 16), bf16",
+        "config": {"workload": WORKLOAD,
                    "global_rows": L_PER_GPU * world, "parallelism": f"sequence-sharded x{world}, NCCL halo "
                    "send/recv of 128 rows per side through hb_comm_halo_exchange" if world > 1 else "single GPU",
                    "l2": "inputs 423 MB per GPU > 126 MB L2 (no flush needed)"},
