@@ -674,7 +674,8 @@ def _dit_clip_runner(model, shape, device, seed: int = 44):
     return clip, (graph, static, eps, x_in)
 
 
-def time_dit_clip(device, ff_quant: str, world: int = 1, clips: int = 3, qkv_quant: str = "none") -> dict:
+def time_dit_clip(device, ff_quant: str, world: int = 1, clips: int = 3, qkv_quant: str = "none",
+                  out_quant: str = "none") -> dict:
     """Config 4: a whole 120 s clip (B=2 CFG pair, 2,584 latents + 64 memory tokens, 24 blocks, 8 pingpong
     steps, random weights) through `hummingbird_b200.dit`, split over `world` GPUs when world > 1: the batch
     rows over two rank groups, then token rows + head pairs inside a group (two NCCL all-to-alls per block).
@@ -684,7 +685,7 @@ def time_dit_clip(device, ff_quant: str, world: int = 1, clips: int = 3, qkv_qua
     from hummingbird_b200.config import DiTConfig
     from hummingbird_b200.dit import DiT, ClipShape
     shape = ClipShape()
-    model = DiT(DiTConfig(ff_quant=ff_quant, qkv_quant=qkv_quant), shape, device,
+    model = DiT(DiTConfig(ff_quant=ff_quant, qkv_quant=qkv_quant, out_quant=out_quant), shape, device,
                 group=dist.group.WORLD if world > 1 else None)
     clip, held = _dit_clip_runner(model, shape, device)
     clip()
@@ -708,6 +709,7 @@ def time_dit_clip(device, ff_quant: str, world: int = 1, clips: int = 3, qkv_qua
                       "steps, 128 context tokens, random weights",
             "mlp": "W8A8" if ff_quant == "w8a8" else "bf16 cuBLAS", "finite": finite,
             "to_qkv": "W8A8 (input quantised by the pre-norm kernel)" if qkv_quant == "w8a8" else "bf16 cuBLAS",
+            "to_out": "W8A8 (attention output quantised per token)" if out_quant == "w8a8" else "bf16 cuBLAS",
             "glue": "fused row kernels (residual + RMSNorm + adaLN, GLU + quantise) and the fused "
                     "differential cross-attention kernel",
             "parallelism": (f"one clip over {world} GPUs: the 2 batch rows over 2 groups of {world // 2} "
@@ -946,7 +948,8 @@ def paths_summary(paths: dict, peaks: dict) -> dict:
         d = paths["w8a8_dit_mlp"]
         out["w8a8_mlp_120s"] = f"GLU in epilogue {d['ms_glu_in_epilogue'] * 1e3:.1f} us vs {d['ms_separate_glu'] * 1e3:.1f} us"
     for key, name in (("dit_120s_clip_bf16_mlp", "dit_120s_bf16"), ("dit_120s_clip_w8a8_mlp", "dit_120s_w8a8"),
-                      ("dit_120s_clip_w8a8_mlp_qkv", "dit_120s_w8a8_qkv")):
+                      ("dit_120s_clip_w8a8_mlp_qkv", "dit_120s_w8a8_qkv"),
+                      ("dit_120s_clip_w8a8_mlp_qkv_out", "dit_120s_w8a8_qkv_out")):
         if key in paths:
             out[name] = f"{paths[key]['ms_per_clip']:.1f} ms/clip"
     if "band_380s_layer" in paths:
@@ -1060,6 +1063,8 @@ def main():
             paths["w8a8_dit_mlp"] = time_w8a8_glu_mlp(device, 30, 5)
             paths["dit_120s_clip_bf16_mlp"] = time_dit_clip(device, "none")
             paths["dit_120s_clip_w8a8_mlp_qkv"] = time_dit_clip(device, "w8a8", qkv_quant="w8a8")
+            paths["dit_120s_clip_w8a8_mlp_qkv_out"] = time_dit_clip(device, "w8a8", qkv_quant="w8a8",
+                                                                    out_quant="w8a8")
         paths["dit_120s_clip_w8a8_mlp"] = time_dit_clip(device, "w8a8", world)
         paths["band_380s_layer"] = time_band_song_layer(device, world, rank, comm=comm)
         paths["song_380s_8_clips"] = time_song(device, world, rank)

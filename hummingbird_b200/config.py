@@ -29,9 +29,11 @@ class DiTConfig:
     fused_min_tokens: int = 0  # the reference gates its TPU kernel at 800 tokens; the B200 kernel has no floor
     ff_quant: Literal["none", "w8a8"] = "none"
     # "w8a8": the self-attention's `to_qkv` as a W8A8 GEMM fed by the pre-norm kernel's per-token int8 output
-    # (glue="cuda", one rank per batch group); `to_out` stays bf16 (its input would need a quantiser pass of its
-    # own, which costs more than the int8 GEMM saves at d = 1024)
+    # (glue="cuda", one rank per batch group)
     qkv_quant: Literal["none", "w8a8"] = "none"
+    # "w8a8": the self-attention's `to_out` as a W8A8 GEMM; its input (the attention output, written per head by
+    # the attention kernel) is quantised per token by a separate quantiser pass (glue="cuda")
+    out_quant: Literal["none", "w8a8"] = "none"
     full_head_rope: bool = False  # True: rotate all 64 dims (the benchmark configs); False: the reference's 32
 
     @property

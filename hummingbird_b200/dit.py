@@ -108,6 +108,8 @@ class DiT:
         self.mem_rows = max(0, min(self.t1, cfg.num_memory_tokens) - self.t0)
         if cfg.qkv_quant == "w8a8" and (self.world > 1 or glue != "cuda"):
             raise ValueError("qkv_quant='w8a8' needs glue='cuda' and one rank per batch group")
+        if cfg.out_quant == "w8a8" and glue != "cuda":
+            raise ValueError("out_quant='w8a8' needs glue='cuda'")
         if (cfg.num_heads // 2) % self.world or self.t1 - self.t0 <= self.mem_rows:
             raise ValueError(f"a clip of {self.seq} tokens and {cfg.num_heads // 2} head pairs does not split "
                              f"over {self.world} ranks (equal pair counts, latent rows on every rank)")
@@ -154,6 +156,8 @@ class DiT:
                 b["self_attn"]["to_qkv_dest"] = b["self_attn"]["to_qkv"][rows].view(self.world, -1, d).transpose(1, 2)
             if cfg.qkv_quant == "w8a8":
                 b["self_attn"]["to_qkv_q"] = W8A8Linear(b["self_attn"]["to_qkv"])
+            if cfg.out_quant == "w8a8":
+                b["self_attn"]["to_out_q"] = W8A8Linear(b["self_attn"]["to_out"])
             if cfg.ff_quant == "w8a8":
                 b["glu_q"] = W8A8Linear(b["glu"]["w"], b["glu"]["b"])
                 b["glu_fused"] = W8A8GluLinear(b["glu"]["w"], b["glu"]["b"])
@@ -277,7 +281,7 @@ class DiT:
                                quantize=qkv_q)
         for i, b in enumerate(self.blocks):
             c = conds[i]
-            y = self._self_attn(x, b["self_attn"], static, lead=h.shape[:-1]) @ b["self_attn"]["to_out"].T
+            y = self._to_out(self._self_attn(x, b["self_attn"], static, lead=h.shape[:-1]), b["self_attn"])
             x = glue.residual_norm(h, y=y, gate=part(c, 2), weight=b["cross_attend_norm_bf"], eps=eps)
             y = self._cross_fused(x, b["cross_attn"], static["cross_kv_rows"][i])
             if self.cfg.ff_quant == "w8a8":  # the MLP's input leaves the norm kernel already quantised per token
@@ -316,6 +320,15 @@ class DiT:
         qkv = par.tokens_to_pairs(send.view(self.world, bsz, rows, -1), self.seq, self.world, self.group)
         att = self.attend(qkv, *args, cfg.num_heads // self.world, cfg.head_dim, cfg.rope_dim // 2, cfg.qk_norm_eps)
         return par.pairs_to_tokens(att, self.seq, self.world, self.rank, self.group)
+
+    def _to_out(self, att, sa):
+        """The self-attention's `to_out` (dit.py:199): a bf16 matmul, or with `out_quant="w8a8"` the attention
+        output quantised per token and a W8A8 GEMM (`to_out` has no bias)."""
+        if self.cfg.out_quant != "w8a8":
+            return att @ sa["to_out"].T
+        lin = sa["to_out_q"]
+        qa, sa_scale = quantize_rows(att.reshape(-1, att.shape[-1]))
+        return w8a8_gemm(qa, sa_scale, lin.qw, lin.sw).view(*att.shape[:-1], -1)
 
     def _cross_fused(self, x, ca, kv_rows):
         """Differential cross-attention (dit.py:203-215) as this library's kernel: `to_q`, then q RMSNorm and

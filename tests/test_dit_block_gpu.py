@@ -117,14 +117,14 @@ def test_dit_block_at_clip_shape_against_oracle(cuda_lib):
     with the W8A8 MLP, against `oracle.dit_block` in float64 on the same bf16 weights and inputs. The cross K/V
     are the block's hoisted, k-normed rows (`prepare_static`; the kernel that builds them is checked in
     `test_cross_gpu.py`). Same bounds as the golden-shape block (measured: 5.0e-3 with the bf16 MLP, 1.9e-2 with
-    the W8A8 MLP)."""
+    the W8A8 MLP); the W8A8 MLP with W8A8 `to_qkv` and `to_out` is held to the W8A8 bound too."""
     from dataclasses import replace
 
     from hummingbird_b200 import _lib
     from hummingbird_b200.config import DiTConfig
     from hummingbird_b200.dit import ClipShape, DiT
     from oracle.dit_block import dit_block
-    cfg = DiTConfig(ff_quant="w8a8")
+    cfg = DiTConfig(ff_quant="w8a8", qkv_quant="w8a8", out_quant="w8a8")
     shape = ClipShape(depth=1, steps=1)
     model = DiT(cfg, shape, "cuda")
     g = torch.Generator(device="cuda").manual_seed(21)
@@ -137,9 +137,9 @@ def test_dit_block_at_clip_shape_against_oracle(cuda_lib):
     with torch.no_grad():
         static = model.prepare_static(cross, glob)
         outs = {}
-        for ff in ("none", "w8a8"):
-            model.cfg = replace(cfg, ff_quant=ff)
-            outs[ff] = to_np(model._blocks_fused(h.clone(), static, gcond))
+        for ff, proj in (("none", "none"), ("w8a8", "none"), ("w8a8", "w8a8")):
+            model.cfg = replace(cfg, ff_quant=ff, qkv_quant=proj, out_quant=proj)
+            outs[(ff, proj)] = to_np(model._blocks_fused(h.clone(), static, gcond))
     torch.cuda.synchronize()
     assert _lib.device_status() == 0
     sa, ca = b["self_attn"], b["cross_attn"]
@@ -152,9 +152,30 @@ def test_dit_block_at_clip_shape_against_oracle(cuda_lib):
     ref = dit_block(to_np(h), p, to_np(gcond), to_np(static["cross_kv_rows"][0]), to_np(model.p["rope_inv_freq"]),
                     np.ones((shape.batch, length)), num_heads=cfg.num_heads, memory=cfg.num_memory_tokens,
                     norm_eps=cfg.norm_eps, qk_eps=cfg.qk_norm_eps)
-    for ff, got in outs.items():
+    for (ff, proj), got in outs.items():
         assert np.all(np.isfinite(got))
         rel_mem, rel_lat = block_rel_errors(got, ref, cfg.num_memory_tokens)
-        print(f"clip shape, {ff} MLP: relative L2 memory rows {rel_mem:.2e}, latent rows {rel_lat:.2e}")
+        print(f"clip shape, {ff} MLP, {proj} to_qkv / to_out: relative L2 memory rows {rel_mem:.2e}, "
+              f"latent rows {rel_lat:.2e}")
         tol = BLOCK_REL_TOL * (2 if ff == "w8a8" else 1)
-        assert rel_mem < tol and rel_lat < tol, (ff, rel_mem, rel_lat)
+        assert rel_mem < tol and rel_lat < tol, (ff, proj, rel_mem, rel_lat)
+
+
+def test_dit_block_with_w8a8_out_projection(cuda_lib):
+    """`out_quant="w8a8"`: the self-attention's `to_out` as a W8A8 GEMM on the per-token quantised attention
+    output (with the W8A8 MLP and W8A8 `to_qkv`), against the reference's fp32 block at the W8A8 bound."""
+    from hummingbird_b200 import _lib
+    from hummingbird_b200.w8a8 import W8A8Linear
+    z = load_golden("dit_block_d256_l136")
+    model, b = _model_with_golden_block(z, "w8a8", "cuda")
+    model.cfg = type(model.cfg)(**{**model.cfg.__dict__, "qkv_quant": "w8a8", "out_quant": "w8a8"})
+    b["self_attn"]["to_qkv_q"] = W8A8Linear(b["self_attn"]["to_qkv"])
+    b["self_attn"]["to_out_q"] = W8A8Linear(b["self_attn"]["to_out"])
+    static = _static(model, z)
+    with torch.no_grad():
+        out = model._blocks_fused(bf16_cuda(z["h_bits"]).clone(), static, bf16_cuda(z["gcond_bits"]))
+    torch.cuda.synchronize()
+    rel_mem, rel_lat = block_rel_errors(to_np(out), z["out_ref"], int(z["memory"]))
+    print(f"W8A8 to_qkv, to_out and MLP: relative L2 memory rows {rel_mem:.2e}, latent rows {rel_lat:.2e}")
+    assert rel_mem < 2 * BLOCK_REL_TOL and rel_lat < 2 * BLOCK_REL_TOL, (rel_mem, rel_lat)
+    assert _lib.device_status() == 0
