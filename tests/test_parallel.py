@@ -1,4 +1,4 @@
-"""CPU (gloo, world_size 2 and 3): the host-side partitioning of the multi-GPU paths — row / pair / clip
+"""CPU (gloo, world sizes 2 to 8): the host-side partitioning of the multi-GPU paths — row / pair / clip
 shards, the halo exchange that feeds sequence-sharded band attention, and the head-pair all-gather."""
 import os
 import socket
@@ -138,11 +138,11 @@ def _dit_worker(rank, world, split_batch):
         assert torch.equal(got, expect)
 
 
-@pytest.mark.parametrize("world,split_batch", [(2, True), (4, True), (2, False), (4, False)])
+@pytest.mark.parametrize("world,split_batch", [(2, True), (4, True), (8, True), (2, False), (4, False)])
 def test_dit_sharding_gloo(world, split_batch):
-    """One clip over 2 / 4 ranks equals one rank: batch rows over rank groups (no collective between them), then
-    token rows + head pairs inside each group (two all-to-alls per block); or token rows + head pairs over all
-    ranks when the batch is not split."""
+    """One clip over 2 / 4 / 8 ranks equals one rank: batch rows over rank groups (no collective between them),
+    then token rows + head pairs inside each group (two all-to-alls per block; at 8 ranks four per batch row, one
+    head pair each); or token rows + head pairs over all ranks when the batch is not split."""
     _run(_dit_worker, world, split_batch)
 
 
