@@ -177,20 +177,21 @@ __device__ __forceinline__ void lds8(const float* src, float (&v)[8]) {
 #endif
 
 // Transform one 128-row tile of two raw sections (q/q_diff or k/k_diff, landed by TMA in the SW128 image)
-// in place: DyT, RoPE, bf16. Four threads own a row; each owns two 8-dim chunks: for rotary dims a chunk
-// and its rotate-half partner (so RoPE needs no exchange and each angle is evaluated once), the remaining
-// chunks in pairs. norm = {alpha, gamma[64], beta[64]} with gamma and beta 16-byte aligned in shared memory
+// in place: DyT, RoPE, bf16. A work item is (chunk pair, row): for rotary dims a chunk and its rotate-half
+// partner (so RoPE needs no exchange and each angle is evaluated once), the remaining chunks in pairs. Items
+// are numbered pair-major, so the 32 lanes of a warp take 32 rows of one pair: the rotary and non-rotary code
+// paths never diverge inside a warp, and the lanes' 16-byte accesses fall in eight different swizzle positions. norm = {alpha, gamma[64], beta[64]} with gamma and beta 16-byte aligned in shared memory
 // (alpha at index 3). The arithmetic runs on packed fp32 pairs: alpha x, gamma t + beta and the rotation.
 __device__ __forceinline__ void prep_inplace(const BandFusedParams& p, int tile, const float* norm,
                                              const float* freqs, uint8_t* buf0, uint8_t* buf1, int pt, int nthreads) {
-  const int sub = pt & 3, rg = pt >> 2, ngroups = nthreads >> 2;
   const int hc8 = p.half >> 3;
-  const bool rot = sub < hc8;
-  const int c0 = rot ? sub : 2 * hc8 + 2 * (sub - hc8);
-  const int c1 = rot ? sub + hc8 : c0 + 1;
   const float alpha = norm[3];
 #pragma unroll 1
-  for (int r = rg; r < kTileRows; r += ngroups) {
+  for (int item = pt; item < 4 * kTileRows; item += nthreads) {
+    const int sub = item >> 7, r = item & (kTileRows - 1);  // warp-uniform sub (nthreads is a multiple of 32)
+    const bool rot = sub < hc8;
+    const int c0 = rot ? sub : 2 * hc8 + 2 * (sub - hc8);
+    const int c1 = rot ? sub + hc8 : c0 + 1;
     const int row = tile * kTileRows + r;
     const bool valid = row < p.rows;
     float cs[8], sn[8];
