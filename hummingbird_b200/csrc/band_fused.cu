@@ -46,6 +46,10 @@ namespace hb {
 namespace {
 
 constexpr int kThreads = 512;
+// Share of the softmax exponentials computed on the FMA pipe (exp2_poly2): key pairs e with
+// (e & kBandPolyMask) == kBandPolyMask, one in eight. The band kernel's preparation stage also loads the XU pipe
+// (tanh, sin, cos); measured at config 2, one in eight 0.3174 ms, one in four 0.3270, one in two 0.3299.
+constexpr int kBandPolyMask = 7;
 // Launched with 128 registers per thread (512 threads, one CTA per SM); the softmax warpgroups take 160,
 // the other two give up to 96: 2 * 160 + 2 * 96 = 4 * 128, the registers the block was launched with. (168 / 88
 // spilled in the preparation warps and measured 3 % slower.)
@@ -546,7 +550,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             ffma2(x0, x1, __uint_as_float(r[c][2 * e]), __uint_as_float(r[c][2 * e + 1]), kScoreScale, kScoreScale,
                   nm, nm);
             float p0, p1;
-            if ((e & kPolyMask) == kPolyMask) {  // a share of the exponentials on the FMA pipe
+            if ((e & kBandPolyMask) == kBandPolyMask) {  // a share of the exponentials on the FMA pipe
               exp2_poly2(x0, x1, p0, p1);
             } else {
               p0 = ex2_approx(x0);
